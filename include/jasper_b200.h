@@ -1,0 +1,153 @@
+/*
+ * jasper_b200.h -- C ABI of the jasper_b200 graph index (B200 / sm_100a).
+ *
+ * Drop-in boundary for Jasper's batched Vamana beam-search path.  Each entry
+ * point replaces one op of the reference's tvm_ffi module
+ * (ffi/jasper_ffi_common.cuh, ffi/jasper_ffi_plain.cu); the reference config
+ * id (f16_r{8,16,32,64}_{l2,ip}) becomes the (n_neighbors, metric) argument
+ * pair.  All pointers are plain C pointers; no framework types cross the ABI.
+ *
+ * Conventions
+ *   - Every function returns JB_OK (0) or a JB_ERR_* code; jb_last_error()
+ *     returns the message of the calling thread's last failure.  Where the
+ *     reference raised (TVM_FFI_ICHECK, std::runtime_error) or called exit(),
+ *     these functions return an error instead.
+ *   - Vectors are IEEE fp16 values passed as uint16_t bit patterns, row-major,
+ *     `row_stride` elements between rows (>= dim).
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream).  Device
+ *     calls are asynchronous on that stream unless stated otherwise.
+ *   - Handles are process-wide and thread-safe to look up; one handle must not
+ *     be built and searched concurrently (as in the reference).
+ */
+#ifndef JASPER_B200_H_
+#define JASPER_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define JB_OK 0
+#define JB_ERR_INVALID_ARGUMENT 1
+#define JB_ERR_INVALID_HANDLE 2
+#define JB_ERR_IO 3
+#define JB_ERR_CUDA 4
+#define JB_ERR_RUNTIME 5
+
+#define JB_METRIC_L2 0
+#define JB_METRIC_IP 1
+
+typedef struct jb_graph_info {
+  uint64_t n_vectors;
+  uint64_t n_deleted;
+  uint64_t next_id;
+  uint32_t dim;
+  uint32_t n_neighbors;
+  int32_t metric;
+  uint32_t medoid;
+  uint32_t global_offset;
+  int32_t on_host;
+  int32_t device;
+} jb_graph_info;
+
+/* Message of this thread's last failing call ("" if none). */
+const char* jb_last_error(void);
+
+/* ABI revision of this header (bumped on incompatible changes). */
+int jb_abi_version(void);
+
+/* Build a graph (reference: ConstructGraph_##id, ffi/jasper_ffi_common.cuh:
+ * 232-261 -> jasper::construct_graph, include/jasper/index/construct.cuh:
+ * 992-1160).  `vectors` may be host (pageable or pinned) or device memory.
+ * The batch cap is min(budget-derived cap, n / 50) exactly as the reference
+ * computes it; where that is 0 (n < 50) one row per batch is used (the
+ * reference loops forever there).  Synchronous. */
+int jb_graph_construct(const uint16_t* vectors, uint64_t n, uint32_t dim, uint32_t row_stride,
+                       uint32_t n_neighbors, int32_t metric, double alpha,
+                       uint64_t workspace_budget_bytes, int32_t on_host, void* stream,
+                       int64_t* out_handle);
+
+/* Load a graph file written by the reference or by jb_graph_save (reference:
+ * LoadGraph_##id, ffi/jasper_ffi_common.cuh:210-219 -> load_graph_from_file,
+ * include/jasper/index/graph.cuh:1425-1651).  Synchronous. */
+int jb_graph_load(const char* path, uint32_t dim, uint32_t n_neighbors, int32_t metric,
+                  int32_t on_host, int64_t* out_handle);
+
+/* Write the reference's on-disk layout (reference: SaveGraph_##id,
+ * ffi/jasper_ffi_common.cuh:221-230 -> save_graph_to_file, graph.cuh:
+ * 1653-1788).  Synchronous. */
+int jb_graph_save(int64_t handle, const char* path);
+
+/* Beam search (reference: Search_##id, ffi/jasper_ffi_common.cuh:302-369 ->
+ * jasper::search, include/jasper/beam_search/api.cuh:57-73).  `queries`,
+ * `out_idx` ([nq][k] int32 stable ids, -1 when fewer than k results) and
+ * `out_dist` ([nq][k] f32, 1e30 when unfilled) are device pointers.
+ * Asynchronous on `stream`. */
+int jb_graph_search(int64_t handle, const uint16_t* queries, uint64_t n_queries,
+                    uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
+                    uint32_t beam_width, uint32_t limit, void* stream);
+
+/* Same search with per-query counters: stats[q][0..3] = expansions, sum of
+ * expanded degrees, distance evaluations, visited-table resets (device
+ * pointer, [n_queries][4] uint32).  Asynchronous. */
+int jb_graph_search_stats(int64_t handle, const uint16_t* queries, uint64_t n_queries,
+                          uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
+                          uint32_t beam_width, uint32_t limit, uint32_t* stats, void* stream);
+
+/* End-to-end search from host buffers: copies the queries in, searches and
+ * copies the results back.  Synchronous (the reference's Search_ also
+ * synchronises, beam_search.cuh:330). */
+int jb_graph_search_host(int64_t handle, const uint16_t* queries, uint64_t n_queries,
+                         uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
+                         uint32_t beam_width, uint32_t limit, void* stream);
+
+/* Release a graph (reference: FreeGraph, ffi/jasper_ffi_plain.cu:15-47). */
+int jb_graph_free(int64_t handle);
+
+/* Metadata (reference: GetNumVectors / GetNumTombstoned / GetNumLive / GetDim,
+ * ffi/jasper_ffi_plain.cu:49-124). */
+int jb_graph_get_info(int64_t handle, jb_graph_info* out);
+
+/* Copy the row with this stable id into `out` (dim fp16; host or device)
+ * (reference: GetVector_##id, ffi/jasper_ffi_common.cuh:263-300). */
+int jb_graph_get_vector(int64_t handle, int64_t stable_id, uint16_t* out);
+
+/* Hand out `count` fresh stable ids into a host int32 array (reference:
+ * ReserveIds, ffi/jasper_ffi_plain.cu:75-93). */
+int jb_graph_reserve_ids(int64_t handle, int64_t count, int32_t* out_ids);
+
+/* Soft-delete rows by id (host int32 array; out-of-range ids ignored); search
+ * never returns them (reference: MarkDeleted_##id ->
+ * include/jasper/index/graph_ops.cuh:93-134). */
+int jb_graph_mark_deleted(int64_t handle, const int32_t* ids, uint64_t n_ids);
+
+/* Create a graph from rows with no edges (host or device rows). */
+int jb_graph_create(const uint16_t* vectors, uint64_t n, uint32_t dim, uint32_t row_stride,
+                    uint32_t n_neighbors, int32_t metric, int32_t on_host, int64_t* out_handle);
+
+/* Replace all adjacency (host arrays [n][R] ids, [n][R] bf16 bit patterns,
+ * [n] counts) and the medoid. */
+int jb_graph_set_edges(int64_t handle, const uint32_t* edges, const uint16_t* edge_dists,
+                       const uint8_t* counts, uint32_t medoid);
+
+/* Read all adjacency into host arrays (same shapes as jb_graph_set_edges). */
+int jb_graph_get_edges(int64_t handle, uint32_t* edges, uint16_t* edge_dists, uint8_t* counts);
+
+/* Make this graph the id range [offset, offset + n) of a larger index: adds
+ * `offset` to every stored neighbour id and to the medoid (reference:
+ * graph::apply_global_offset, include/jasper/index/graph.cuh:801-827). */
+int jb_graph_apply_global_offset(int64_t handle, uint32_t offset);
+
+/* Merge per-shard top-k lists (device pointers, [n_shards][n_queries][k])
+ * into the global top-k by (distance, id), on `stream`.  Used after the shards
+ * of a range-sharded index are gathered on one GPU; no reference counterpart
+ * (the reference has no multi-GPU path). */
+int jb_merge_topk(const int32_t* shard_idx, const float* shard_dist, uint32_t n_shards,
+                  uint64_t n_queries, uint32_t k, int32_t* out_idx, float* out_dist, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JASPER_B200_H_ */

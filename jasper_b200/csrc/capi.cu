@@ -1,0 +1,427 @@
+// capi.cu -- extern "C" entry points of libjasper_b200.so (include/jasper_b200.h).
+//
+// The handle table mirrors the reference's (ffi/jasper_ffi_plain.cu:10-13):
+// a process-wide map from int64 handle to graph, guarded by one mutex that is
+// held only for lookups; the op bodies run unlocked.
+#include <cuda_runtime.h>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <unordered_map>
+#include <vector>
+#include "../../include/jasper_b200.h"
+#include "construct.cuh"
+#include "jb_graph.h"
+#include "merge.cuh"
+#include "search.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+std::unordered_map<int64_t, std::shared_ptr<jb::Graph>> g_graphs;
+int64_t g_next_handle = 0;
+std::mutex g_mutex;
+
+struct InvalidHandle : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+struct IoError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+template <typename F>
+int guarded(F&& f) {
+  try {
+    f();
+    g_last_error.clear();
+    return JB_OK;
+  } catch (const InvalidHandle& e) {
+    return fail(JB_ERR_INVALID_HANDLE, e.what());
+  } catch (const std::invalid_argument& e) {
+    return fail(JB_ERR_INVALID_ARGUMENT, e.what());
+  } catch (const IoError& e) {
+    return fail(JB_ERR_IO, e.what());
+  } catch (const std::exception& e) {
+    std::string m = e.what();
+    if (m.find("Failed to open") != std::string::npos || m.find("Short read") != std::string::npos ||
+        m.find("graph file") != std::string::npos)
+      return fail(JB_ERR_IO, m);
+    return fail(JB_ERR_RUNTIME, m);
+  } catch (...) {
+    return fail(JB_ERR_RUNTIME, "unknown error");
+  }
+}
+
+std::shared_ptr<jb::Graph> lookup(int64_t h) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  auto it = g_graphs.find(h);
+  if (it == g_graphs.end()) throw InvalidHandle("Invalid handle: " + std::to_string(h));
+  return it->second;
+}
+
+int64_t insert(std::shared_ptr<jb::Graph> g) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  int64_t h = g_next_handle++;
+  g_graphs[h] = std::move(g);
+  return h;
+}
+
+void cuda_check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+// Runs with the graph's device current, restoring the caller's afterwards.
+struct DeviceScope {
+  int prev = -1;
+  explicit DeviceScope(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+void check_metric(int32_t metric) {
+  if (metric != JB_METRIC_L2 && metric != JB_METRIC_IP)
+    throw std::invalid_argument("metric must be JB_METRIC_L2 or JB_METRIC_IP");
+}
+
+// Device search over queries with any row stride: rows whose stride is not
+// the padded dim are first packed into a padded scratch copy.
+void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint32_t row_stride,
+                 int32_t* out_idx, float* out_dist, uint32_t k, uint32_t bw, uint32_t limit,
+                 uint32_t* stats, cudaStream_t st) {
+  if (nq == 0) return;
+  if (nq > 0x7FFFFFFFull) throw std::invalid_argument("too many queries");
+  if (k == 0) throw std::invalid_argument("k must be > 0");
+  if (row_stride < g.dim) throw std::invalid_argument("row_stride < dim");
+  if (out_idx == nullptr || out_dist == nullptr || queries == nullptr)
+    throw std::invalid_argument("null pointer argument");
+  const uint16_t* q = queries;
+  void* packed = nullptr;
+  void* counter = nullptr;
+  const bool aligned = (reinterpret_cast<uintptr_t>(queries) % 16) == 0;
+  if (row_stride != g.dpad || !aligned) {
+    cuda_check(cudaMallocAsync(&packed, size_t(nq) * g.dpad * 2, st), "alloc packed queries");
+    cuda_check(cudaMemsetAsync(packed, 0, size_t(nq) * g.dpad * 2, st), "clear packed queries");
+    cuda_check(cudaMemcpy2DAsync(packed, size_t(g.dpad) * 2, queries, size_t(row_stride) * 2,
+                                 size_t(g.dim) * 2, nq, cudaMemcpyDefault, st),
+               "pack queries");
+    q = static_cast<const uint16_t*>(packed);
+  }
+  cuda_check(cudaMallocAsync(&counter, jb::kSearchScratchBytes, st), "alloc search scratch");
+  cuda_check(cudaMemsetAsync(counter, 0, jb::kSearchScratchBytes, st), "clear search scratch");
+  jb::SearchArgs a{};
+  a.g = g.view();
+  a.queries = q;
+  a.nq = uint32_t(nq);
+  a.k = k;
+  a.bw = bw;
+  a.limit = limit;
+  a.max_result_size = 2048;  // jasper::search_params default (beam_search/api.cuh:17)
+  a.out_idx = out_idx;
+  a.out_dist = out_dist;
+  a.work_counter = static_cast<uint32_t*>(counter);
+  a.stats = stats;
+  try {
+    jb::launch_search(a, st);
+  } catch (...) {
+    cudaFreeAsync(counter, st);
+    if (packed) cudaFreeAsync(packed, st);
+    throw;
+  }
+  cuda_check(cudaFreeAsync(counter, st), "free search scratch");
+  if (packed) cuda_check(cudaFreeAsync(packed, st), "free packed queries");
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* jb_last_error(void) { return g_last_error.c_str(); }
+
+int jb_abi_version(void) { return 1; }
+
+int jb_graph_create(const uint16_t* vectors, uint64_t n, uint32_t dim, uint32_t row_stride,
+                    uint32_t n_neighbors, int32_t metric, int32_t on_host, int64_t* out_handle) {
+  return guarded([&] {
+    check_metric(metric);
+    if (out_handle == nullptr) throw std::invalid_argument("out_handle is null");
+    if (n > 0 && vectors == nullptr) throw std::invalid_argument("vectors is null");
+    if (row_stride < dim) throw std::invalid_argument("row_stride < dim");
+    if (n >= 0x7FFFFFFFull) throw std::invalid_argument("too many vectors");
+    auto g = std::make_shared<jb::Graph>();
+    jb::graph_allocate(*g, dim, n_neighbors, metric, uint32_t(n), on_host != 0);
+    try {
+      jb::graph_upload_rows(*g, vectors, row_stride);
+    } catch (...) {
+      jb::graph_free(*g);
+      throw;
+    }
+    *out_handle = insert(g);
+  });
+}
+
+int jb_graph_construct(const uint16_t* vectors, uint64_t n, uint32_t dim, uint32_t row_stride,
+                       uint32_t n_neighbors, int32_t metric, double alpha,
+                       uint64_t workspace_budget_bytes, int32_t on_host, void* stream,
+                       int64_t* out_handle) {
+  return guarded([&] {
+    check_metric(metric);
+    if (out_handle == nullptr) throw std::invalid_argument("out_handle is null");
+    if (n > 0 && vectors == nullptr) throw std::invalid_argument("vectors is null");
+    if (row_stride < dim) throw std::invalid_argument("row_stride < dim");
+    if (n >= 0x7FFFFFFFull) throw std::invalid_argument("too many vectors");
+    auto g = std::make_shared<jb::Graph>();
+    jb::graph_allocate(*g, dim, n_neighbors, metric, uint32_t(n), on_host != 0);
+    try {
+      jb::graph_upload_rows(*g, vectors, row_stride);
+      uint32_t mb = jb::reference_max_batch_size(workspace_budget_bytes, uint32_t(n), n_neighbors);
+      jb::construct_graph(*g, float(alpha), mb, static_cast<cudaStream_t>(stream));
+    } catch (...) {
+      jb::graph_free(*g);
+      throw;
+    }
+    *out_handle = insert(g);
+  });
+}
+
+int jb_graph_load(const char* path, uint32_t dim, uint32_t n_neighbors, int32_t metric,
+                  int32_t on_host, int64_t* out_handle) {
+  return guarded([&] {
+    check_metric(metric);
+    if (path == nullptr || out_handle == nullptr) throw std::invalid_argument("null argument");
+    auto g = std::make_shared<jb::Graph>();
+    jb::graph_load_file(*g, path, dim, n_neighbors, metric, on_host != 0);
+    *out_handle = insert(g);
+  });
+}
+
+int jb_graph_save(int64_t handle, const char* path) {
+  return guarded([&] {
+    if (path == nullptr) throw std::invalid_argument("path is null");
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    cuda_check(cudaDeviceSynchronize(), "sync before save");
+    jb::graph_save_file(*g, path);
+  });
+}
+
+int jb_graph_search(int64_t handle, const uint16_t* queries, uint64_t n_queries,
+                    uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
+                    uint32_t beam_width, uint32_t limit, void* stream) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    search_impl(*g, queries, n_queries, row_stride, out_idx, out_dist, k, beam_width, limit,
+                nullptr, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int jb_graph_search_stats(int64_t handle, const uint16_t* queries, uint64_t n_queries,
+                          uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
+                          uint32_t beam_width, uint32_t limit, uint32_t* stats, void* stream) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    search_impl(*g, queries, n_queries, row_stride, out_idx, out_dist, k, beam_width, limit, stats,
+                static_cast<cudaStream_t>(stream));
+  });
+}
+
+int jb_graph_search_host(int64_t handle, const uint16_t* queries, uint64_t n_queries,
+                         uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
+                         uint32_t beam_width, uint32_t limit, void* stream) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (n_queries == 0) return;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t qbytes = size_t(n_queries) * g->dpad * 2;
+    const size_t obytes = size_t(n_queries) * k * 4;
+    void *dq = nullptr, *di = nullptr, *dd = nullptr;
+    cuda_check(cudaMallocAsync(&dq, qbytes, st), "alloc queries");
+    cuda_check(cudaMallocAsync(&di, obytes, st), "alloc out idx");
+    cuda_check(cudaMallocAsync(&dd, obytes, st), "alloc out dist");
+    try {
+      if (row_stride == g->dpad) {
+        cuda_check(cudaMemcpyAsync(dq, queries, qbytes, cudaMemcpyHostToDevice, st), "copy queries");
+      } else {
+        cuda_check(cudaMemsetAsync(dq, 0, qbytes, st), "clear queries");
+        cuda_check(cudaMemcpy2DAsync(dq, size_t(g->dpad) * 2, queries, size_t(row_stride) * 2,
+                                     size_t(g->dim) * 2, n_queries, cudaMemcpyHostToDevice, st),
+                   "copy queries");
+      }
+      search_impl(*g, static_cast<uint16_t*>(dq), n_queries, g->dpad, static_cast<int32_t*>(di),
+                  static_cast<float*>(dd), k, beam_width, limit, nullptr, st);
+      cuda_check(cudaMemcpyAsync(out_idx, di, obytes, cudaMemcpyDeviceToHost, st), "copy idx");
+      cuda_check(cudaMemcpyAsync(out_dist, dd, obytes, cudaMemcpyDeviceToHost, st), "copy dist");
+    } catch (...) {
+      cudaFreeAsync(dq, st); cudaFreeAsync(di, st); cudaFreeAsync(dd, st);
+      cudaStreamSynchronize(st);
+      throw;
+    }
+    cudaFreeAsync(dq, st); cudaFreeAsync(di, st); cudaFreeAsync(dd, st);
+    cuda_check(cudaStreamSynchronize(st), "search");
+  });
+}
+
+int jb_graph_free(int64_t handle) {
+  return guarded([&] {
+    std::shared_ptr<jb::Graph> g;
+    {
+      std::lock_guard<std::mutex> lock(g_mutex);
+      auto it = g_graphs.find(handle);
+      if (it == g_graphs.end()) throw InvalidHandle("Invalid handle: " + std::to_string(handle));
+      g = it->second;
+      g_graphs.erase(it);
+    }
+    DeviceScope ds(g->device);
+    cudaDeviceSynchronize();
+    jb::graph_free(*g);
+  });
+}
+
+int jb_graph_get_info(int64_t handle, jb_graph_info* out) {
+  return guarded([&] {
+    if (out == nullptr) throw std::invalid_argument("out is null");
+    auto g = lookup(handle);
+    out->n_vectors = g->n;
+    out->n_deleted = g->n_deleted;
+    out->next_id = g->next_id;
+    out->dim = g->dim;
+    out->n_neighbors = g->R;
+    out->metric = g->metric;
+    out->medoid = g->medoid;
+    out->global_offset = g->global_offset;
+    out->on_host = g->on_host ? 1 : 0;
+    out->device = g->device;
+  });
+}
+
+int jb_graph_get_vector(int64_t handle, int64_t stable_id, uint16_t* out) {
+  return guarded([&] {
+    if (out == nullptr) throw std::invalid_argument("out is null");
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (stable_id < 0) throw std::invalid_argument("stable id must be non-negative");
+    int64_t slot = -1;
+    if (g->ids_identity) {
+      if (uint64_t(stable_id) < g->n) slot = stable_id;
+    } else {
+      std::vector<uint32_t> ids(g->n);
+      cuda_check(cudaMemcpy(ids.data(), g->slot_to_id, size_t(g->n) * 4, cudaMemcpyDefault), "ids");
+      for (uint32_t i = 0; i < g->n; i++)
+        if (ids[i] == uint32_t(stable_id)) { slot = i; break; }
+    }
+    if (slot < 0) throw std::invalid_argument("Stable id " + std::to_string(stable_id) + " not found");
+    cuda_check(cudaMemcpy(out, g->vec + size_t(slot) * g->dpad, size_t(g->dim) * 2, cudaMemcpyDefault),
+               "copy vector");
+  });
+}
+
+int jb_graph_reserve_ids(int64_t handle, int64_t count, int32_t* out_ids) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    if (count < 0) throw std::invalid_argument("count must be >= 0");
+    if (count > 0 && out_ids == nullptr) throw std::invalid_argument("out_ids is null");
+    const uint64_t start = g->next_id;
+    g->next_id += uint64_t(count);
+    for (int64_t i = 0; i < count; i++) out_ids[i] = int32_t(start + uint64_t(i));
+  });
+}
+
+int jb_graph_mark_deleted(int64_t handle, const int32_t* ids, uint64_t n_ids) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (n_ids > 0 && ids == nullptr) throw std::invalid_argument("ids is null");
+    std::vector<uint32_t> words((size_t(g->n) + 31) / 32);
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    cuda_check(cudaMemcpy(words.data(), g->deleted, words.size() * 4, cudaMemcpyDefault), "bits");
+    for (uint64_t i = 0; i < n_ids; i++) {
+      const int64_t id = ids[i];
+      if (id < 0 || uint64_t(id) >= g->n) continue;  // ids are slots while ids are identity
+      uint32_t& w = words[size_t(id) >> 5];
+      const uint32_t bit = 1u << (id & 31);
+      if (!(w & bit)) { w |= bit; g->n_deleted++; }
+    }
+    cuda_check(cudaMemcpy(g->deleted, words.data(), words.size() * 4, cudaMemcpyDefault), "bits");
+  });
+}
+
+int jb_graph_set_edges(int64_t handle, const uint32_t* edges, const uint16_t* edge_dists,
+                       const uint8_t* counts, uint32_t medoid) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (!edges || !edge_dists || !counts) throw std::invalid_argument("null argument");
+    if (medoid - g->global_offset >= g->n && g->n > 0) throw std::invalid_argument("medoid out of range");
+    const size_t nr = size_t(g->n) * g->R;
+    cuda_check(cudaMemcpy(g->edges, edges, nr * 4, cudaMemcpyDefault), "set edges");
+    cuda_check(cudaMemcpy(g->edist, edge_dists, nr * 2, cudaMemcpyDefault), "set dists");
+    cuda_check(cudaMemcpy(g->counts, counts, g->n, cudaMemcpyDefault), "set counts");
+    g->medoid = medoid;
+  });
+}
+
+int jb_graph_get_edges(int64_t handle, uint32_t* edges, uint16_t* edge_dists, uint8_t* counts) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (!edges || !edge_dists || !counts) throw std::invalid_argument("null argument");
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    const size_t nr = size_t(g->n) * g->R;
+    cuda_check(cudaMemcpy(edges, g->edges, nr * 4, cudaMemcpyDefault), "get edges");
+    cuda_check(cudaMemcpy(edge_dists, g->edist, nr * 2, cudaMemcpyDefault), "get dists");
+    cuda_check(cudaMemcpy(counts, g->counts, g->n, cudaMemcpyDefault), "get counts");
+  });
+}
+
+int jb_graph_apply_global_offset(int64_t handle, uint32_t offset) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (uint64_t(offset) + g->n >= 0x7FFFFFFFull) throw std::invalid_argument("offset too large");
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    const size_t nr = size_t(g->n) * g->R;
+    std::vector<uint32_t> e(nr);
+    std::vector<uint8_t> c(g->n);
+    cuda_check(cudaMemcpy(e.data(), g->edges, nr * 4, cudaMemcpyDefault), "edges");
+    cuda_check(cudaMemcpy(c.data(), g->counts, g->n, cudaMemcpyDefault), "counts");
+    const uint32_t delta = offset - g->global_offset;
+    for (uint32_t i = 0; i < g->n; i++)
+      for (uint32_t j = 0; j < c[i]; j++) {
+        uint32_t& v = e[size_t(i) * g->R + j];
+        if (v != 0xFFFFFFFFu) v += delta;
+      }
+    cuda_check(cudaMemcpy(g->edges, e.data(), nr * 4, cudaMemcpyDefault), "edges");
+    g->medoid += delta;
+    g->global_offset = offset;
+  });
+}
+
+int jb_merge_topk(const int32_t* shard_idx, const float* shard_dist, uint32_t n_shards,
+                  uint64_t n_queries, uint32_t k, int32_t* out_idx, float* out_dist, void* stream) {
+  return guarded([&] {
+    if (n_queries == 0) return;
+    if (!shard_idx || !shard_dist || !out_idx || !out_dist) throw std::invalid_argument("null argument");
+    jb::launch_merge_topk(shard_idx, shard_dist, n_shards, n_queries, k, out_idx, out_dist,
+                          static_cast<cudaStream_t>(stream));
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,466 @@
+// construct.cu -- batched Vamana construction (greedy search + RobustPrune).
+//
+// Follows construct_graph / construction_round / process_batch of the
+// reference (include/jasper/index/construct.cuh:743-1160): rows are inserted
+// in id order in batches of 1, 2, 4, ... up to max_batch_size; for each batch
+//   (a) beam search from the medoid for every batch row (L = beam = 64,
+//       limit 256, expansion list capped at 256), recording the expansion
+//       order with exact distances -- the same warp-per-query kernel as the
+//       query search (search.cu) in range mode;
+//   (b) candidates = the row's existing edges (stored bf16 distances) plus the
+//       expansion list minus the row itself, sorted by (distance, id)
+//       (merge_candidates_kernel, construct.cuh:280-377);
+//   (c) RobustPrune(alpha): walk the sorted candidates, keep c unless a kept
+//       s has d(c, s) * alpha < d(row, c), stop at R (construct.cuh:379-473);
+//   (d) reverse edges (target = new neighbour, sink = batch row) are sorted
+//       by (target, sink) and split into one group per target
+//       (fill_reverse_edges + thrust semisort, construct.cuh:475-558);
+//   (e) for every target: existing edges plus the sinks with fresh distances,
+//       sorted, pruned again and written back (construct.cuh:560-741).
+//
+// Device design: one warp per batch row / per target, candidates sorted by a
+// bitonic network in shared memory, the pruned candidate's row held in
+// registers in the 4-lane distance layout while each 4-lane tile tests it
+// against two kept rows at a time; the scan over kept rows stops at the first
+// pass that prunes (the reference evaluates all of them; the OR is the same).
+// Every phase is stream-ordered with no host round trip, so a whole build is
+// a sequence of asynchronous launches.
+//
+// One deliberate difference: when a target collects more than 256 + R
+// candidates in (e), the reference keeps whichever ones its shared-memory
+// atomics place first; this code keeps the 256 + R best by (distance, id).
+// Below that cap (the common case) the two are identical.
+#include <cub/device/device_radix_sort.cuh>
+#include <stdexcept>
+#include <string>
+#include "construct.cuh"
+#include "jb_common.cuh"
+#include "search.cuh"
+
+namespace jb {
+namespace {
+
+constexpr uint32_t kMaxCandSort = 512;  // sort capacity per warp
+
+void check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+// Candidate-row distances for the prune: the candidate row is the tile's
+// "query".  nchunks is dim / 8 (the reference passes the unpadded dim to
+// compute_distance in the prune kernels, construct.cuh:437-439).
+template <int MAXC, int METRIC>
+struct RowReg {
+  uint4 q[MAXC > 0 ? MAXC : 1];
+  const uint16_t* qs;  // shared-memory copy when MAXC == 0
+  __device__ __forceinline__ void load(const GraphView& g, uint32_t id, int nchunks, int lane,
+                                       uint16_t* smem_row) {
+    const uint4* row = reinterpret_cast<const uint4*>(g.vec + size_t(id - g.global_offset) * g.dpad);
+    const int s = lane & 3;
+    if constexpr (MAXC > 0) {
+#pragma unroll
+      for (int i = 0; i < MAXC; i++) {
+        int c = s + 4 * i;
+        q[i] = c < nchunks ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      __syncwarp();
+      uint4* dst = reinterpret_cast<uint4*>(smem_row);
+      for (int c = lane; c < int(g.dpad / 8); c += 32) dst[c] = ldg16(row + c);
+      __syncwarp();
+      qs = smem_row;
+    }
+  }
+  __device__ __forceinline__ float dist(const GraphView& g, uint32_t id, bool active,
+                                        int nchunks, int s) const {
+    const uint4* row = reinterpret_cast<const uint4*>(g.vec + size_t(id - g.global_offset) * g.dpad);
+    float acc = 0.f;
+    if constexpr (MAXC > 0 && METRIC == kL2) {
+      uint4 x[MAXC];
+#pragma unroll
+      for (int i = 0; i < MAXC; i++) {
+        int c = s + 4 * i;
+        x[i] = (active && c < nchunks) ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < MAXC; i++)
+        if (s + 4 * i < nchunks) acc = l2_chunk(q[i], x[i], acc);
+      return tile4_sum(acc);
+    } else if constexpr (METRIC == kL2) {
+      const uint4* q4 = reinterpret_cast<const uint4*>(qs);
+      for (int c = s; c < nchunks; c += 4) {
+        uint4 r = active ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+        acc = l2_chunk(q4[c], r, acc);
+      }
+      return tile4_sum(acc);
+    } else {
+      const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qs);
+      const uint32_t* r32 = reinterpret_cast<const uint32_t*>(row);
+      const int w = s >> 1;
+      const int nck = int(g.dpad / 8);
+      for (int c = 0; c < nck; c++) {
+        uint32_t rlo = active ? __ldg(r32 + 4 * c + w) : 0u;
+        uint32_t rhi = active ? __ldg(r32 + 4 * c + 2 + w) : 0u;
+        acc = ip_pair(q32[4 * c + w], q32[4 * c + 2 + w], rlo, rhi, s, acc);
+      }
+      return -tile4_sum(acc);
+    }
+  }
+};
+
+struct PruneSmem {
+  uint64_t* cand;   // [kMaxCandSort]
+  uint32_t* sel;    // [64]
+  float* sel_d;     // [64]
+  uint16_t* row;    // [dpad] (shared-memory row path)
+};
+
+__host__ __device__ inline size_t prune_warp_bytes(uint32_t dpad) {
+  return kMaxCandSort * 8 + 64 * 4 + 64 * 4 + ((size_t(dpad) * 2 + 15) & ~size_t(15));
+}
+
+__device__ __forceinline__ PruneSmem prune_carve(char* base) {
+  PruneSmem p;
+  p.cand = reinterpret_cast<uint64_t*>(base);
+  p.sel = reinterpret_cast<uint32_t*>(p.cand + kMaxCandSort);
+  p.sel_d = reinterpret_cast<float*>(p.sel + 64);
+  p.row = reinterpret_cast<uint16_t*>(p.sel_d + 64);
+  return p;
+}
+
+// Sort cand[0, nc) ascending (pads the power-of-two tail with the max key).
+__device__ __forceinline__ void sort_cands(uint64_t* cand, int nc, int lane) {
+  int n = 32;
+  while (n < nc) n <<= 1;
+  for (int i = nc + lane; i < n; i += 32) cand[i] = kKeyMax;
+  __syncwarp();
+  warp_sort_smem(cand, n, lane);
+}
+
+// RobustPrune over sorted candidate pair keys; writes the row of `self`.
+template <int MAXC, int METRIC>
+__device__ void prune_and_write(const GraphView& g, uint32_t self, PruneSmem& sm, int nc,
+                                float alpha, int lane) {
+  const int tile = lane >> 2, s = lane & 3;
+  const int nchunks = int(g.dim / 8);
+  const uint32_t R = g.R;
+  uint32_t ns = 0;
+  RowReg<MAXC, METRIC> cr;
+  for (int i = 0; i < nc; i++) {
+    if (ns >= R) break;
+    const uint64_t key = sm.cand[i];
+    const uint32_t cid = pair_id(key);
+    if (cid == self || cid == kInvalid) continue;
+    const float cd = key_dist(key);
+    cr.load(g, cid, nchunks, lane, sm.row);
+    bool pruned = false;
+    for (uint32_t base = 0; base < ns; base += 16) {
+      const uint32_t j0 = base + tile, j1 = base + tile + 8;
+      const bool a0 = j0 < ns, a1 = j1 < ns;
+      const float d0 = cr.dist(g, a0 ? sm.sel[j0] : cid, a0, nchunks, s);
+      const float d1 = cr.dist(g, a1 ? sm.sel[j1] : cid, a1, nchunks, s);
+      const bool p = (a0 && d0 * alpha < cd) || (a1 && d1 * alpha < cd);
+      if (__any_sync(kFull, p)) { pruned = true; break; }
+    }
+    if (!pruned) {
+      if (lane == 0) { sm.sel[ns] = cid; sm.sel_d[ns] = cd; }
+      ns++;
+      __syncwarp();
+    }
+  }
+  __syncwarp();
+  const uint32_t l = self - g.global_offset;
+  for (uint32_t i = lane; i < ns; i += 32) {
+    g.edges[size_t(l) * R + i] = sm.sel[i];
+    g.edist[size_t(l) * R + i] = float_to_bf16_bits(sm.sel_d[i]);
+  }
+  if (lane == 0) g.counts[l] = uint8_t(ns);
+  __syncwarp();
+}
+
+// (b) + (c) for batch rows [off, off + bs).
+template <int MAXC, int METRIC>
+__global__ void __launch_bounds__(128) batch_prune_kernel(GraphView g, uint32_t off, uint32_t bs,
+                                                          const uint32_t* vis_idx,
+                                                          const float* vis_dist,
+                                                          const uint32_t* vis_cnt, uint32_t mrs,
+                                                          float alpha) {
+  extern __shared__ __align__(16) char smem_raw[];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  PruneSmem sm = prune_carve(smem_raw + prune_warp_bytes(g.dpad) * wid);
+  const uint32_t R = g.R;
+  const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
+  for (uint32_t b = blockIdx.x * (blockDim.x >> 5) + wid; b < bs; b += nwarps) {
+    const uint32_t gid = off + b;
+    const uint32_t l = gid - g.global_offset;
+    int nc = 0;
+    const uint32_t ne = g.counts[l];
+    for (uint32_t base = 0; base < ne; base += 32) {
+      const uint32_t e = base + lane;
+      uint32_t id = e < ne ? g.edges[size_t(l) * R + e] : kInvalid;
+      const bool ok = e < ne && id != kInvalid;
+      const uint32_t bal = __ballot_sync(kFull, ok);
+      if (ok) {
+        const float d = bf16_bits_to_float(g.edist[size_t(l) * R + e]);
+        sm.cand[nc + __popc(bal & ((1u << lane) - 1u))] = make_pair_key(d, id);
+      }
+      nc += __popc(bal);
+    }
+    const uint32_t vc = vis_cnt[b];
+    for (uint32_t base = 0; base < vc; base += 32) {
+      const uint32_t i = base + lane;
+      uint32_t id = i < vc ? vis_idx[size_t(b) * mrs + i] : kInvalid;
+      const bool ok = i < vc && id != gid && id != kInvalid;
+      const uint32_t bal = __ballot_sync(kFull, ok);
+      if (ok) sm.cand[nc + __popc(bal & ((1u << lane) - 1u))] =
+          make_pair_key(vis_dist[size_t(b) * mrs + i], id);
+      nc += __popc(bal);
+    }
+    __syncwarp();
+    sort_cands(sm.cand, nc, lane);
+    prune_and_write<MAXC, METRIC>(g, gid, sm, nc, alpha, lane);
+  }
+}
+
+// (d) reverse pairs: key = target << 32 | sink, empty slots = max key.
+__global__ void fill_reverse_kernel(GraphView g, uint32_t off, uint32_t bs, uint64_t* keys) {
+  const size_t total = size_t(bs) * g.R;
+  for (size_t t = size_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+       t += size_t(gridDim.x) * blockDim.x) {
+    const uint32_t b = uint32_t(t / g.R), e = uint32_t(t % g.R);
+    const uint32_t gid = off + b;
+    const uint32_t l = gid - g.global_offset;
+    uint64_t k = kKeyMax;
+    if (e < g.counts[l]) k = (uint64_t(g.edges[size_t(l) * g.R + e]) << 32) | gid;
+    keys[t] = k;
+  }
+}
+
+__global__ void group_starts_kernel(const uint64_t* keys, size_t total, uint32_t* starts,
+                                    uint32_t* n_groups) {
+  for (size_t i = size_t(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += size_t(gridDim.x) * blockDim.x) {
+    const uint64_t k = keys[i];
+    if (k == kKeyMax) continue;
+    if (i == 0 || (keys[i - 1] >> 32) != (k >> 32)) starts[atomicAdd(n_groups, 1u)] = uint32_t(i);
+  }
+}
+
+// (e) one warp per reverse-edge target.
+template <int MAXC, int METRIC>
+__global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const uint64_t* keys,
+                                                            size_t total, const uint32_t* starts,
+                                                            const uint32_t* n_groups, float alpha) {
+  extern __shared__ __align__(16) char smem_raw[];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int tile = lane >> 2, s = lane & 3;
+  PruneSmem sm = prune_carve(smem_raw + prune_warp_bytes(g.dpad) * wid);
+  const uint32_t R = g.R;
+  const uint32_t cap = 256 + R;  // MAX_CANDS of construct.cuh:574
+  const uint32_t ng = *n_groups;
+  const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
+  const int nchunks = int(g.dim / 8);
+  for (uint32_t gi = blockIdx.x * (blockDim.x >> 5) + wid; gi < ng; gi += nwarps) {
+    const size_t start = starts[gi];
+    const uint32_t t = uint32_t(keys[start] >> 32);
+    const uint32_t l = t - g.global_offset;
+    int nc = 0;
+    const uint32_t ne = g.counts[l];
+    for (uint32_t base = 0; base < ne; base += 32) {
+      const uint32_t e = base + lane;
+      uint32_t id = e < ne ? g.edges[size_t(l) * R + e] : kInvalid;
+      const bool ok = e < ne && id != kInvalid;
+      const uint32_t bal = __ballot_sync(kFull, ok);
+      if (ok) sm.cand[nc + __popc(bal & ((1u << lane) - 1u))] =
+          make_pair_key(bf16_bits_to_float(g.edist[size_t(l) * R + e]), id);
+      nc += __popc(bal);
+    }
+    RowReg<MAXC, METRIC> tr;
+    tr.load(g, t, nchunks, lane, sm.row);
+    // The group is the contiguous run of keys with this target.
+    size_t end = start;
+    for (;;) {
+      const size_t i = end + lane;
+      const bool in = i < total && keys[i] != kKeyMax && uint32_t(keys[i] >> 32) == t;
+      const uint32_t bal = __ballot_sync(kFull, in);
+      if (bal == kFull) { end += 32; continue; }
+      end += __ffs(~bal) - 1;
+      break;
+    }
+    // Sinks with fresh distances, 16 per pass (two rows per 4-lane tile).
+    for (size_t i = start; i < end; i += 16) {
+      if (nc + 16 > int(kMaxCandSort)) {  // keep the `cap` best so far
+        sort_cands(sm.cand, nc, lane);
+        if (nc > int(cap)) nc = int(cap);
+      }
+      const size_t i0 = i + tile, i1 = i + tile + 8;
+      const uint32_t s0 = i0 < end ? uint32_t(keys[i0]) : kInvalid;
+      const uint32_t s1 = i1 < end ? uint32_t(keys[i1]) : kInvalid;
+      const bool a0 = i0 < end && s0 != t && s0 != kInvalid;
+      const bool a1 = i1 < end && s1 != t && s1 != kInvalid;
+      const float d0 = tr.dist(g, a0 ? s0 : t, a0, nchunks, s);
+      const float d1 = tr.dist(g, a1 ? s1 : t, a1, nchunks, s);
+      const uint32_t b0 = __ballot_sync(kFull, a0 && s == 0);
+      const uint32_t b1 = __ballot_sync(kFull, a1 && s == 0);
+      if (s == 0) {
+        const uint32_t lt = (1u << lane) - 1u;
+        if (a0) sm.cand[nc + __popc(b0 & lt)] = make_pair_key(d0, s0);
+        if (a1) sm.cand[nc + __popc(b0) + __popc(b1 & lt)] = make_pair_key(d1, s1);
+      }
+      nc += __popc(b0) + __popc(b1);
+      __syncwarp();
+    }
+    __syncwarp();
+    sort_cands(sm.cand, nc, lane);
+    if (nc > int(cap)) nc = int(cap);
+    prune_and_write<MAXC, METRIC>(g, t, sm, nc, alpha, lane);
+  }
+}
+
+template <int MAXC, int METRIC>
+struct Kernels {
+  static void prune(const GraphView& g, uint32_t off, uint32_t bs, const BuildWorkspace& ws,
+                    float alpha, cudaStream_t st) {
+    const size_t smem = prune_warp_bytes(g.dpad) * 4;
+    auto k = batch_prune_kernel<MAXC, METRIC>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    const uint32_t blocks = (bs + 3) / 4;
+    k<<<blocks, 128, smem, st>>>(g, off, bs, ws.vis_idx, ws.vis_dist, ws.vis_cnt, kBuildMaxResult,
+                                 alpha);
+  }
+  static void reverse(const GraphView& g, size_t total, const BuildWorkspace& ws, float alpha,
+                      cudaStream_t st) {
+    const size_t smem = prune_warp_bytes(g.dpad) * 4;
+    auto k = reverse_prune_kernel<MAXC, METRIC>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 128, smem);
+    if (per_sm < 1) per_sm = 1;
+    size_t blocks = size_t(sms) * per_sm;
+    const size_t need = (total + 3) / 4;
+    if (blocks > need) blocks = need;
+    if (blocks == 0) blocks = 1;
+    k<<<uint32_t(blocks), 128, smem, st>>>(g, ws.rev_sorted, total, ws.group_starts,
+                                           ws.counters + 1, alpha);
+  }
+};
+
+template <int METRIC>
+void dispatch_prune(const GraphView& g, uint32_t off, uint32_t bs, const BuildWorkspace& ws,
+                    float alpha, cudaStream_t st, bool reverse, size_t total) {
+  const uint32_t nchunks = g.dim / 8;
+  auto run = [&](auto kernels) {
+    if (reverse) decltype(kernels)::reverse(g, total, ws, alpha, st);
+    else decltype(kernels)::prune(g, off, bs, ws, alpha, st);
+  };
+  if (METRIC == kIP) return run(Kernels<0, METRIC>{});
+  if (nchunks <= 4) return run(Kernels<1, METRIC>{});
+  if (nchunks <= 8) return run(Kernels<2, METRIC>{});
+  if (nchunks <= 12) return run(Kernels<3, METRIC>{});
+  if (nchunks <= 16) return run(Kernels<4, METRIC>{});
+  if (nchunks <= 32) return run(Kernels<8, METRIC>{});
+  return run(Kernels<0, METRIC>{});
+}
+
+}  // namespace
+
+uint32_t reference_max_batch_size(uint64_t budget_bytes, uint32_t n, uint32_t R) {
+  // graph_construct_workspace::max_batch_size_for_budget (construct.cuh:233-258)
+  // with L = 64, max_result_size = 256, entry = 8 B, edge_pair = 8 B, index = 4 B,
+  // then min(., n / 50) as ConstructGraph does (ffi/jasper_ffi_common.cuh:245-248).
+  const uint64_t L = 64, mrs = 256;
+  const uint64_t per_item = 8 * L + 8 * mrs + 4 + 8 * (mrs + R) + 4 + 8ull * R + 4ull * R + 4ull * R;
+  const uint64_t fixed = 4;
+  uint64_t b = budget_bytes <= fixed ? 0 : (budget_bytes - fixed) / per_item;
+  if (b > 0xFFFFFFFFull) b = 0xFFFFFFFFull;
+  uint32_t batch = uint32_t(b);
+  uint32_t cap = n / 50;
+  return batch < cap ? batch : cap;
+}
+
+void workspace_allocate(BuildWorkspace& ws, uint32_t max_batch, uint32_t R) {
+  ws = BuildWorkspace{};
+  ws.max_batch = max_batch;
+  const size_t pairs = size_t(max_batch) * R;
+  check(cudaMalloc(&ws.vis_idx, size_t(max_batch) * kBuildMaxResult * 4), "alloc visited ids");
+  check(cudaMalloc(&ws.vis_dist, size_t(max_batch) * kBuildMaxResult * 4), "alloc visited dists");
+  check(cudaMalloc(&ws.vis_cnt, size_t(max_batch) * 4), "alloc visited counts");
+  check(cudaMalloc(&ws.rev_keys, pairs * 8), "alloc reverse pairs");
+  check(cudaMalloc(&ws.rev_sorted, pairs * 8), "alloc sorted reverse pairs");
+  check(cudaMalloc(&ws.group_starts, pairs * 4), "alloc group starts");
+  check(cudaMalloc(&ws.counters, 256), "alloc counters");
+  size_t tmp = 0;
+  cub::DeviceRadixSort::SortKeys(nullptr, tmp, ws.rev_keys, ws.rev_sorted, int(pairs), 0, 64);
+  ws.sort_tmp_bytes = tmp;
+  check(cudaMalloc(&ws.sort_tmp, tmp ? tmp : 16), "alloc sort scratch");
+}
+
+void workspace_free(BuildWorkspace& ws) {
+  cudaFree(ws.vis_idx); cudaFree(ws.vis_dist); cudaFree(ws.vis_cnt);
+  cudaFree(ws.rev_keys); cudaFree(ws.rev_sorted); cudaFree(ws.group_starts);
+  cudaFree(ws.counters); cudaFree(ws.sort_tmp);
+  ws = BuildWorkspace{};
+}
+
+void process_batch(Graph& graph, BuildWorkspace& ws, uint32_t off, uint32_t bs, float alpha,
+                   cudaStream_t st) {
+  const GraphView g = graph.view();
+  check(cudaMemsetAsync(ws.counters, 0, 256, st), "clear counters");
+  SearchArgs a{};
+  a.g = g;
+  a.use_range = 1;
+  a.query_start = off;
+  a.nq = bs;
+  a.k = kBuildL;
+  a.bw = kBuildL;
+  a.limit = kBuildLimit;
+  a.max_result_size = kBuildMaxResult;
+  a.vis_idx = ws.vis_idx;
+  a.vis_dist = ws.vis_dist;
+  a.vis_cnt = ws.vis_cnt;
+  a.work_counter = ws.counters;
+  launch_search(a, st);
+  if (g.metric == kIP) dispatch_prune<kIP>(g, off, bs, ws, alpha, st, false, 0);
+  else dispatch_prune<kL2>(g, off, bs, ws, alpha, st, false, 0);
+  const size_t total = size_t(bs) * g.R;
+  const uint32_t fb = uint32_t(std::min<size_t>((total + 255) / 256, 4096));
+  fill_reverse_kernel<<<fb, 256, 0, st>>>(g, off, bs, ws.rev_keys);
+  size_t tmp = ws.sort_tmp_bytes;
+  check(cub::DeviceRadixSort::SortKeys(ws.sort_tmp, tmp, ws.rev_keys, ws.rev_sorted, int(total), 0,
+                                       64, st),
+        "sort reverse pairs");
+  group_starts_kernel<<<fb, 256, 0, st>>>(ws.rev_sorted, total, ws.group_starts, ws.counters + 1);
+  if (g.metric == kIP) dispatch_prune<kIP>(g, off, bs, ws, alpha, st, true, total);
+  else dispatch_prune<kL2>(g, off, bs, ws, alpha, st, true, total);
+  check(cudaGetLastError(), "construct batch launch");
+}
+
+void construct_graph(Graph& graph, float alpha, uint32_t max_batch, cudaStream_t st) {
+  if (max_batch == 0) max_batch = 1;
+  if (graph.n == 0) return;
+  BuildWorkspace ws;
+  workspace_allocate(ws, max_batch, graph.R);
+  try {
+    uint32_t count = 0, bs = 1;
+    while (count < graph.n) {
+      bs = std::min(bs, graph.n - count);
+      bs = std::min(bs, max_batch);
+      process_batch(graph, ws, graph.global_offset + count, bs, alpha, st);
+      count += bs;
+      if (bs < max_batch) bs = std::min(max_batch, bs * 2);
+    }
+    check(cudaStreamSynchronize(st), "construct");
+  } catch (...) {
+    cudaStreamSynchronize(st);
+    workspace_free(ws);
+    throw;
+  }
+  workspace_free(ws);
+}
+
+}  // namespace jb

@@ -1,0 +1,247 @@
+// graph.cu -- allocation, upload and the on-disk format of a jasper_b200 graph.
+//
+// The file format is the reference's, byte for byte
+// (include/jasper/index/graph.cuh:1653-1788, save_graph_to_file):
+//   [u64 total_file_size][u64 n][u64 medoid][u64 bytes_per_node]
+//   n records of: dim x fp16 (unpadded) | u8 edge_count |
+//                 R x u32 ids | R x bf16 distances | u32 slot_to_id
+//   ceil(n / 8) bytes of deletion bitmask (bit i = slot i), then u64 next_id.
+// The loader also accepts the three older record layouts the reference
+// reader detects by bytes_per_node (graph.cuh:1460-1479): legacy (no id, no
+// deletion), +deleted byte, +deleted byte +id.  Unlike the reference, a bad
+// path or a short file raises instead of calling exit().
+#include <cuda_runtime.h>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <stdexcept>
+#include <vector>
+#include "jb_graph.h"
+
+namespace jb {
+namespace {
+
+void check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+template <typename T>
+T* alloc_array(size_t count, bool on_host, const char* what) {
+  void* p = nullptr;
+  size_t bytes = count * sizeof(T);
+  if (bytes == 0) bytes = 16;
+  if (on_host) check(cudaHostAlloc(&p, bytes, cudaHostAllocMapped | cudaHostAllocPortable), what);
+  else check(cudaMalloc(&p, bytes), what);
+  return static_cast<T*>(p);
+}
+
+void free_array(void* p, bool on_host) {
+  if (!p) return;
+  if (on_host) cudaFreeHost(p); else cudaFree(p);
+}
+
+void copy_to(void* dst, const void* src, size_t bytes) {
+  check(cudaMemcpy(dst, src, bytes, cudaMemcpyDefault), "graph copy");
+}
+
+}  // namespace
+
+void graph_allocate(Graph& g, uint32_t dim, uint32_t R, int metric, uint32_t n, bool on_host) {
+  if (dim == 0) throw std::invalid_argument("dim must be > 0");
+  if (R == 0 || R > 64) throw std::invalid_argument("n_neighbors must be in [1, 64]");
+  if (n >= 0x7FFFFFFFu) throw std::invalid_argument("graphs are limited to 2^31 - 1 rows");
+  g = Graph{};
+  check(cudaGetDevice(&g.device), "cudaGetDevice");
+  g.dim = dim;
+  g.dpad = pad_dim(dim);
+  g.R = R;
+  g.metric = metric;
+  g.n = n;
+  g.on_host = on_host;
+  g.next_id = n;
+  try {
+    g.vec = alloc_array<uint16_t>(size_t(n) * g.dpad, on_host, "alloc vectors");
+    g.edges = alloc_array<uint32_t>(size_t(n) * R, on_host, "alloc edges");
+    g.edist = alloc_array<uint16_t>(size_t(n) * R, on_host, "alloc edge distances");
+    g.counts = alloc_array<uint8_t>(n, on_host, "alloc edge counts");
+    g.slot_to_id = alloc_array<uint32_t>(n, on_host, "alloc slot ids");
+    g.deleted = alloc_array<uint32_t>((size_t(n) + 31) / 32, on_host, "alloc deletion bits");
+    if (on_host) {
+      memset(g.edges, 0xFF, size_t(n) * R * 4);
+      memset(g.edist, 0, size_t(n) * R * 2);
+      memset(g.counts, 0, n);
+      memset(g.deleted, 0, ((size_t(n) + 31) / 32) * 4);
+    } else {
+      check(cudaMemset(g.edges, 0xFF, size_t(n) * R * 4), "memset edges");
+      check(cudaMemset(g.edist, 0, size_t(n) * R * 2), "memset dists");
+      check(cudaMemset(g.counts, 0, n), "memset counts");
+      check(cudaMemset(g.deleted, 0, ((size_t(n) + 31) / 32) * 4), "memset deleted");
+    }
+  } catch (...) {
+    graph_free(g);
+    throw;
+  }
+}
+
+void graph_free(Graph& g) {
+  free_array(g.vec, g.on_host);
+  free_array(g.edges, g.on_host);
+  free_array(g.edist, g.on_host);
+  free_array(g.counts, g.on_host);
+  free_array(g.slot_to_id, g.on_host);
+  free_array(g.deleted, g.on_host);
+  g.vec = nullptr; g.edges = nullptr; g.edist = nullptr; g.counts = nullptr;
+  g.slot_to_id = nullptr; g.deleted = nullptr;
+  g.n = 0;
+}
+
+void graph_upload_rows(Graph& g, const uint16_t* rows, uint32_t stride) {
+  const size_t n = g.n;
+  if (n == 0) return;
+  // Padded row array: one 2-D copy puts each dim-element row at stride dpad;
+  // the pad lanes are zeroed first so padded distances stay exact.
+  if (g.dpad != g.dim) {
+    if (g.on_host) memset(g.vec, 0, n * g.dpad * 2);
+    else check(cudaMemset(g.vec, 0, n * g.dpad * 2), "memset pad");
+  }
+  check(cudaMemcpy2D(g.vec, size_t(g.dpad) * 2, rows, size_t(stride) * 2, size_t(g.dim) * 2, n,
+                     cudaMemcpyDefault),
+        "upload rows");
+  std::vector<uint32_t> ids(n);
+  for (size_t i = 0; i < n; i++) ids[i] = uint32_t(i);
+  copy_to(g.slot_to_id, ids.data(), n * 4);
+  g.ids_identity = true;
+}
+
+void graph_load_file(Graph& g, const std::string& path, uint32_t dim, uint32_t R, int metric,
+                     bool on_host) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f.is_open()) throw std::runtime_error("Failed to open " + path + " for graph load");
+  uint64_t hdr[4];
+  f.read(reinterpret_cast<char*>(hdr), sizeof(hdr));
+  if (f.gcount() != sizeof(hdr)) throw std::runtime_error("graph file too short: " + path);
+  const uint64_t n = hdr[1], medoid = hdr[2], bpn = hdr[3];
+  const uint64_t base = 2ull * dim + 1 + 6ull * R;
+  const bool bitpacked = bpn == base + 4;
+  const bool inline_del = bpn == base + 1 || bpn == base + 5;
+  const bool has_id = bpn == base + 5 || bitpacked;
+  if (!(bpn == base || bitpacked || inline_del))
+    throw std::runtime_error("graph file " + path + ": bytes_per_node " + std::to_string(bpn) +
+                             " does not match dim=" + std::to_string(dim) +
+                             " n_neighbors=" + std::to_string(R));
+  if (n >= 0x7FFFFFFFull) throw std::runtime_error("graph file has too many rows");
+  graph_allocate(g, dim, R, metric, uint32_t(n), on_host);
+  g.medoid = uint32_t(medoid);
+  try {
+    const uint32_t dpad = g.dpad;
+    const size_t chunk = size_t(1) << 18;
+    std::vector<char> raw(chunk * bpn);
+    std::vector<uint16_t> hv(chunk * dpad);
+    std::vector<uint32_t> he(chunk * R), hid(chunk);
+    std::vector<uint16_t> hd(chunk * R);
+    std::vector<uint8_t> hc(chunk);
+    std::vector<uint8_t> del_bits((n + 7) / 8, 0);
+    bool identity = true;
+    for (uint64_t start = 0; start < n; start += chunk) {
+      const size_t cnt = size_t(std::min<uint64_t>(chunk, n - start));
+      f.read(raw.data(), std::streamsize(cnt * bpn));
+      if (size_t(f.gcount()) != cnt * bpn)
+        throw std::runtime_error("Short read in graph file " + path);
+      std::fill(hv.begin(), hv.begin() + cnt * dpad, 0);
+      for (size_t i = 0; i < cnt; i++) {
+        const char* p = raw.data() + i * bpn;
+        memcpy(&hv[i * dpad], p, 2ull * dim);
+        p += 2ull * dim;
+        hc[i] = uint8_t(*p);
+        p += 1;
+        memcpy(&he[i * R], p, 4ull * R);
+        p += 4ull * R;
+        memcpy(&hd[i * R], p, 2ull * R);
+        p += 2ull * R;
+        if (inline_del) {
+          if (*p) del_bits[(start + i) >> 3] |= uint8_t(1u << ((start + i) & 7));
+          p += 1;
+        }
+        uint32_t id = uint32_t(start + i);
+        if (has_id) memcpy(&id, p, 4);
+        hid[i] = id;
+        if (id != uint32_t(start + i)) identity = false;
+      }
+      copy_to(g.vec + start * dpad, hv.data(), cnt * dpad * 2);
+      copy_to(g.edges + start * R, he.data(), cnt * R * 4);
+      copy_to(g.edist + start * R, hd.data(), cnt * R * 2);
+      copy_to(g.counts + start, hc.data(), cnt);
+      copy_to(g.slot_to_id + start, hid.data(), cnt * 4);
+    }
+    if (bitpacked) {
+      f.read(reinterpret_cast<char*>(del_bits.data()), std::streamsize(del_bits.size()));
+      if (size_t(f.gcount()) != del_bits.size())
+        throw std::runtime_error("Short read of deletion bitmask in " + path);
+    }
+    uint64_t next_id = n;
+    if (has_id) {
+      f.read(reinterpret_cast<char*>(&next_id), 8);
+      if (f.gcount() != 8) next_id = n;
+    }
+    std::vector<uint32_t> words((n + 31) / 32, 0);
+    uint64_t n_del = 0;
+    for (uint64_t i = 0; i < n; i++)
+      if ((del_bits[i >> 3] >> (i & 7)) & 1u) {
+        words[i >> 5] |= 1u << (i & 31);
+        n_del++;
+      }
+    copy_to(g.deleted, words.data(), words.size() * 4);
+    g.n_deleted = n_del;
+    g.next_id = next_id;
+    g.ids_identity = identity;
+  } catch (...) {
+    graph_free(g);
+    throw;
+  }
+}
+
+void graph_save_file(const Graph& g, const std::string& path) {
+  std::ofstream f(path, std::ios::binary);
+  if (!f.is_open()) throw std::runtime_error("Failed to open " + path + " for graph save");
+  const uint64_t n = g.n, dim = g.dim, R = g.R;
+  const uint64_t bpn = 2 * dim + 1 + 6 * R + 4;
+  const uint64_t del_bytes = (n + 7) / 8;
+  uint64_t hdr[4] = {4 * 8 + n * bpn + del_bytes + 8, n, g.medoid, bpn};
+  f.write(reinterpret_cast<const char*>(hdr), sizeof(hdr));
+  const size_t chunk = size_t(1) << 18;
+  std::vector<uint16_t> hv(chunk * g.dpad), hd(chunk * R);
+  std::vector<uint32_t> he(chunk * R), hid(chunk);
+  std::vector<uint8_t> hc(chunk);
+  std::vector<char> out(chunk * bpn);
+  for (uint64_t start = 0; start < n; start += chunk) {
+    const size_t cnt = size_t(std::min<uint64_t>(chunk, n - start));
+    copy_to(hv.data(), g.vec + start * g.dpad, cnt * g.dpad * 2);
+    copy_to(he.data(), g.edges + start * R, cnt * R * 4);
+    copy_to(hd.data(), g.edist + start * R, cnt * R * 2);
+    copy_to(hc.data(), g.counts + start, cnt);
+    copy_to(hid.data(), g.slot_to_id + start, cnt * 4);
+    for (size_t i = 0; i < cnt; i++) {
+      char* p = out.data() + i * bpn;
+      memcpy(p, &hv[i * g.dpad], 2 * dim); p += 2 * dim;
+      *p = char(hc[i]); p += 1;
+      memcpy(p, &he[i * R], 4 * R); p += 4 * R;
+      memcpy(p, &hd[i * R], 2 * R); p += 2 * R;
+      memcpy(p, &hid[i], 4);
+    }
+    f.write(out.data(), std::streamsize(cnt * bpn));
+  }
+  std::vector<uint32_t> words((n + 31) / 32);
+  copy_to(words.data(), g.deleted, words.size() * 4);
+  std::vector<uint8_t> bits(del_bytes, 0);
+  for (uint64_t i = 0; i < n; i++)
+    if ((words[i >> 5] >> (i & 31)) & 1u) bits[i >> 3] |= uint8_t(1u << (i & 7));
+  f.write(reinterpret_cast<const char*>(bits.data()), std::streamsize(bits.size()));
+  uint64_t next_id = g.next_id;
+  f.write(reinterpret_cast<const char*>(&next_id), 8);
+  if (!f.good()) throw std::runtime_error("write failed for " + path);
+}
+
+}  // namespace jb

@@ -1,0 +1,158 @@
+// jb_common.cuh -- device helpers shared by the search and build kernels.
+//
+// Beam entries are 64-bit keys that sort in the reference's CustomPairLess
+// order (include/jasper/beam_search/device_kernels.cuh:132-151: distance
+// ascending, then 31-bit id ascending):
+//     key = ordered_bits(dist) << 32 | id << 1 | visited
+// ordered_bits() maps an IEEE float to an unsigned integer with the same
+// order, so one 64-bit integer compare is the reference comparator.  The
+// visited flag lives in bit 0 below the id: it never decides the order of two
+// distinct ids, and the beam never holds two copies of one id.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+namespace jb {
+
+constexpr uint32_t kFull = 0xFFFFFFFFu;
+constexpr uint32_t kInvalid = 0xFFFFFFFFu;
+constexpr uint64_t kKeyMax = ~0ull;
+
+__device__ __forceinline__ uint32_t ordered_bits(float d) {
+  d = d + 0.0f;  // -0.0 -> +0.0: the reference compares floats, where they tie
+  uint32_t u = __float_as_uint(d);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float from_ordered_bits(uint32_t u) {
+  u = (u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u;
+  return __uint_as_float(u);
+}
+
+__device__ __forceinline__ uint64_t make_key(float d, uint32_t id) {
+  return (uint64_t(ordered_bits(d)) << 32) | (uint64_t(id & 0x7FFFFFFFu) << 1);
+}
+__device__ __forceinline__ uint32_t key_id(uint64_t k) { return uint32_t(k) >> 1; }
+__device__ __forceinline__ float key_dist(uint64_t k) { return from_ordered_bits(uint32_t(k >> 32)); }
+__device__ __forceinline__ bool key_visited(uint64_t k) { return k & 1ull; }
+
+// Candidate pairs of the build (id is a full 32-bit id there, no flag).
+__device__ __forceinline__ uint64_t make_pair_key(float d, uint32_t id) {
+  return (uint64_t(ordered_bits(d)) << 32) | uint64_t(id);
+}
+__device__ __forceinline__ uint32_t pair_id(uint64_t k) { return uint32_t(k); }
+
+// Read-only 16-byte gather through the non-coherent path.
+__device__ __forceinline__ uint4 ldg16(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+// One 16-byte chunk (8 halves) of the L2 sum, element order 0..7, each term
+// fused as fma(d, d, acc): the reference's per-lane accumulation
+// (include/jasper/distance/distance.cuh:131-141).
+__device__ __forceinline__ float l2_chunk(uint4 a, uint4 b, float acc) {
+  const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+  const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int w = 0; w < 4; w++) {
+    __half2 ha = *reinterpret_cast<const __half2*>(&aw[w]);
+    __half2 hb = *reinterpret_cast<const __half2*>(&bw[w]);
+    float2 fa = __half22float2(ha);
+    float2 fb = __half22float2(hb);
+    float d0 = __fsub_rn(fa.x, fb.x);
+    acc = __fmaf_rn(d0, d0, acc);
+    float d1 = __fsub_rn(fa.y, fb.y);
+    acc = __fmaf_rn(d1, d1, acc);
+  }
+  return acc;
+}
+
+// The two elements (s, s+4) of one chunk that lane s of a 4-lane tile owns
+// in the reference's inner-product walk (distance.cuh:95-106: element i goes
+// to lane i % 4, in increasing i).
+__device__ __forceinline__ float ip_pair(uint32_t qlo, uint32_t qhi, uint32_t rlo,
+                                         uint32_t rhi, int s, float acc) {
+  const int sh = (s & 1) * 16;
+  float q0 = __half2float(__ushort_as_half((unsigned short)(qlo >> sh)));
+  float r0 = __half2float(__ushort_as_half((unsigned short)(rlo >> sh)));
+  acc = __fmaf_rn(q0, r0, acc);
+  float q1 = __half2float(__ushort_as_half((unsigned short)(qhi >> sh)));
+  float r1 = __half2float(__ushort_as_half((unsigned short)(rhi >> sh)));
+  acc = __fmaf_rn(q1, r1, acc);
+  return acc;
+}
+
+// Butterfly over a 4-lane tile, identical to cg::reduce(tile, x, plus):
+// mask 2 then mask 1, each step out = out + partner
+// (cooperative_groups/details/coalesced_reduce.h).
+__device__ __forceinline__ float tile4_sum(float x) {
+  x = __fadd_rn(x, __shfl_xor_sync(kFull, x, 2));
+  x = __fadd_rn(x, __shfl_xor_sync(kFull, x, 1));
+  return x;
+}
+
+// Warp-wide bitonic sort of 64 keys held two per lane (element p = r*32+lane).
+__device__ __forceinline__ void warp_sort64(uint64_t& v0, uint64_t& v1, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      if (j == 32) {
+        uint64_t lo = v0 < v1 ? v0 : v1, hi = v0 < v1 ? v1 : v0;
+        v0 = lo; v1 = hi;
+      } else {
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+          uint64_t& v = r ? v1 : v0;
+          const int p = r * 32 + lane;
+          uint64_t o = __shfl_xor_sync(kFull, v, j);
+          const bool up = (p & k) == 0;
+          const bool low = (lane & j) == 0;
+          const bool take_min = (low == up);
+          v = take_min ? (v < o ? v : o) : (v < o ? o : v);
+        }
+      }
+    }
+  }
+}
+
+// Bitonic sort of n (power of two, <= 32 * 32) keys in shared memory by one warp.
+__device__ __forceinline__ void warp_sort_smem(uint64_t* a, int n, int lane) {
+  for (int k = 2; k <= n; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = lane; i < n; i += 32) {
+        int p = i ^ j;
+        if (p > i) {
+          uint64_t x = a[i], y = a[p];
+          bool up = (i & k) == 0;
+          if ((x > y) == up) { a[i] = y; a[p] = x; }
+        }
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// Number of elements of sorted a[0, n) strictly below x.
+__device__ __forceinline__ int lower_rank(const uint64_t* a, int n, uint64_t x) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    int mid = (lo + hi) >> 1;
+    if (a[mid] < x) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
+  return __uint_as_float(uint32_t(b) << 16);
+}
+__device__ __forceinline__ uint16_t float_to_bf16_bits(float f) {
+  __nv_bfloat16 h = __float2bfloat16_rn(f);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+
+}  // namespace jb

@@ -1,0 +1,403 @@
+// search.cu -- warp-per-query Vamana beam search for sm_100a.
+//
+// Replaces beam_search_kernel (include/jasper/beam_search/beam_search.cuh:
+// 25-259) and its device phases (device_kernels.cuh:23-288) with a design that
+// returns the same top-k on the same graph:
+//
+//  * one warp owns one query (several warps per CTA, queries handed out by an
+//    atomic counter), so every phase synchronises with __syncwarp only;
+//  * the beam is a sorted array of 64-bit keys (jb_common.cuh) in shared
+//    memory, double-buffered; a round merges the sorted new candidates into it
+//    by rank (each element's output slot = own index + rank in the other
+//    list) and clips to beam_width, which is the reference's
+//    sort + dedup + clip_k on a buffer without duplicates;
+//  * a per-query open-addressing hash set in shared memory remembers every id
+//    whose distance was computed, so a neighbour is evaluated at most once.
+//    The reference instead re-appends duplicates and removes them after a
+//    full-buffer sort.  This does not change the traversal: a re-appended id
+//    that is still in the beam is dropped by the reference's stable dedup
+//    (the beam copy comes first and keeps its visited bit), and one that was
+//    clipped before has at least beam_width strictly smaller entries ahead of
+//    it and is clipped again.  When the table passes half full it is cleared
+//    and refilled with the current beam, so beam members are always found;
+//    forgotten clipped ids are merely recomputed, and clipped again;
+//  * out-of-range neighbours (the global_offset range test of
+//    device_kernels.cuh:110-121) are dropped instead of becoming visited
+//    sentinels: a sentinel sorts after every real entry, is never expanded and
+//    is never output, so dropping it changes nothing;
+//  * the query sits in registers in the layout of the reference's 4-lane
+//    distance tile: lane s of a tile holds 16-byte chunks s, s+4, ...; every
+//    candidate row is gathered with 16-byte non-coherent loads, two rows per
+//    tile in flight, and the per-lane sums and the tile reduction follow the
+//    reference's order exactly, so distances are bit-identical.
+//
+// Loop bounds follow beam_search.cuh:129-203: at most limit + 1 rounds; a
+// round expands the first unvisited beam entry; when the expansion count
+// reaches max_result_size the loop stops before adding that node's neighbours.
+#include <stdexcept>
+#include <string>
+#include "jb_common.cuh"
+#include "search.cuh"
+
+namespace jb {
+namespace {
+
+constexpr uint32_t kHashEmpty = 0xFFFFFFFFu;
+
+struct WarpSmem {
+  uint64_t* beam0;
+  uint64_t* beam1;
+  uint64_t* cand_keys;  // [64]
+  uint32_t* cand_ids;   // [64]
+  uint32_t* hash;       // [1 << hbits]
+  uint16_t* query;      // [dpad] (shared-memory query path only)
+};
+
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+__host__ __device__ inline size_t warp_smem_bytes(uint32_t bwcap, uint32_t hbits, uint32_t dpad,
+                                                  bool smem_query) {
+  size_t b = 0;
+  b += 2 * sizeof(uint64_t) * bwcap;
+  b += sizeof(uint64_t) * 64;
+  b += sizeof(uint32_t) * 64;
+  b += sizeof(uint32_t) * (size_t(1) << hbits);
+  b = align16(b);
+  if (smem_query) b += align16(sizeof(uint16_t) * dpad);
+  return b;
+}
+
+__device__ __forceinline__ WarpSmem carve(char* base, uint32_t bwcap, uint32_t hbits) {
+  WarpSmem s;
+  s.beam0 = reinterpret_cast<uint64_t*>(base);
+  s.beam1 = s.beam0 + bwcap;
+  s.cand_keys = s.beam1 + bwcap;
+  s.cand_ids = reinterpret_cast<uint32_t*>(s.cand_keys + 64);
+  s.hash = s.cand_ids + 64;
+  size_t off = align16(reinterpret_cast<char*>(s.hash + (size_t(1) << hbits)) - base);
+  s.query = reinterpret_cast<uint16_t*>(base + off);
+  return s;
+}
+
+// Insert id; true when it was absent.  The caller keeps the table at most
+// half full, so the probe sequence always ends at an empty slot.
+__device__ __forceinline__ bool hash_insert(uint32_t* h, uint32_t hbits, uint32_t id) {
+  const uint32_t mask = (1u << hbits) - 1u;
+  uint32_t slot = (id * 0x9E3779B1u) >> (32 - hbits);
+  for (uint32_t probe = 0; probe <= mask; probe++) {
+    uint32_t prev = atomicCAS(&h[slot], kHashEmpty, id);
+    if (prev == kHashEmpty) return true;
+    if (prev == id) return false;
+    slot = (slot + 1) & mask;
+  }
+  return true;
+}
+
+// Distance of one query to rows of the graph, per 4-lane tile.
+// REG: query chunks in registers (L2, dpad <= 32 * MAXC * 8 / 4).
+template <int MAXC, int METRIC>
+struct QueryReg {
+  uint4 q[MAXC];
+  __device__ __forceinline__ void load(const uint4* row, int nchunks, int s) {
+#pragma unroll
+    for (int i = 0; i < MAXC; i++) {
+      int c = s + 4 * i;
+      q[i] = c < nchunks ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+    }
+  }
+  // Distances of two rows at once (r1 may alias r0).  Returns tile-reduced sums.
+  __device__ __forceinline__ void dist2(const uint4* r0, const uint4* r1, bool a0, bool a1,
+                                        int nchunks, int s, float& d0, float& d1) const {
+    uint4 x[MAXC], y[MAXC];
+#pragma unroll
+    for (int i = 0; i < MAXC; i++) {
+      int c = s + 4 * i;
+      x[i] = (a0 && c < nchunks) ? ldg16(r0 + c) : make_uint4(0, 0, 0, 0);
+      y[i] = (a1 && c < nchunks) ? ldg16(r1 + c) : make_uint4(0, 0, 0, 0);
+    }
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXC; i++) {
+      int c = s + 4 * i;
+      if (c < nchunks) {
+        acc0 = l2_chunk(q[i], x[i], acc0);
+        acc1 = l2_chunk(q[i], y[i], acc1);
+      }
+    }
+    d0 = tile4_sum(acc0);
+    d1 = tile4_sum(acc1);
+  }
+};
+
+// Shared-memory query: any dpad, L2 or inner product.
+template <int METRIC>
+__device__ __forceinline__ float dist_smemq(const uint16_t* qs, const uint4* row, bool active,
+                                            int nchunks, int s) {
+  float acc = 0.f;
+  if (METRIC == kL2) {
+    const uint4* q4 = reinterpret_cast<const uint4*>(qs);
+    for (int c = s; c < nchunks; c += 4) {
+      uint4 r = active ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+      acc = l2_chunk(q4[c], r, acc);
+    }
+  } else {
+    // element i belongs to lane i % 4: in chunk c lane s takes elements s and
+    // s + 4, i.e. half (s & 1) of 32-bit words (s >> 1) and 2 + (s >> 1).
+    const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qs);
+    const uint32_t* r32 = reinterpret_cast<const uint32_t*>(row);
+    const int w = s >> 1;
+    for (int c = 0; c < nchunks; c++) {
+      uint32_t rlo = active ? __ldg(r32 + 4 * c + w) : 0u;
+      uint32_t rhi = active ? __ldg(r32 + 4 * c + 2 + w) : 0u;
+      acc = ip_pair(q32[4 * c + w], q32[4 * c + 2 + w], rlo, rhi, s, acc);
+    }
+  }
+  acc = tile4_sum(acc);
+  return METRIC == kL2 ? acc : -acc;
+}
+
+template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC>
+__global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
+  constexpr bool kRegQ = (MAXC > 0);
+  extern __shared__ __align__(16) char smem_raw[];
+  const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
+  const uint32_t dpad = a.g.dpad;
+  const size_t per_warp = warp_smem_bytes(BWCAP, HBITS, dpad, !kRegQ);
+  WarpSmem sm = carve(smem_raw + per_warp * wid, BWCAP, HBITS);
+  const int tile = lane >> 2, s = lane & 3;
+  const int nchunks = int(dpad / 8);
+  const GraphView& g = a.g;
+  const uint32_t hsize = 1u << HBITS;
+  const uint32_t R = g.R;
+  const uint32_t bw = a.bw;
+
+  for (;;) {
+    uint32_t q = 0;
+    if (lane == 0) q = atomicAdd(a.work_counter, 1u);
+    q = __shfl_sync(kFull, q, 0);
+    if (q >= a.nq) break;
+
+    const uint16_t* qrow = a.use_range
+        ? g.vec + size_t(a.query_start + q - g.global_offset) * dpad
+        : a.queries + size_t(q) * dpad;
+    QueryReg<(MAXC > 0 ? MAXC : 1), METRIC> qr;
+    if constexpr (kRegQ) {
+      qr.load(reinterpret_cast<const uint4*>(qrow), nchunks, s);
+    } else {
+      const uint4* src = reinterpret_cast<const uint4*>(qrow);
+      uint4* dst = reinterpret_cast<uint4*>(sm.query);
+      for (int c = lane; c < nchunks; c += 32) dst[c] = ldg16(src + c);
+    }
+    for (uint32_t i = lane; i < hsize; i += 32) sm.hash[i] = kHashEmpty;
+    __syncwarp();
+
+    // Evaluate candidates sm.cand_ids[0, m) into sm.cand_keys (sorted on exit).
+    auto evaluate_and_sort = [&](int m) {
+      for (int base = 0; base < m; base += 16) {
+        const int i0 = base + tile, i1 = base + tile + 8;
+        const bool a0 = i0 < m, a1 = i1 < m;
+        const uint32_t id0 = a0 ? sm.cand_ids[i0] : g.global_offset;
+        const uint32_t id1 = a1 ? sm.cand_ids[i1] : id0;
+        const uint4* r0 = reinterpret_cast<const uint4*>(g.vec + size_t(id0 - g.global_offset) * dpad);
+        const uint4* r1 = reinterpret_cast<const uint4*>(g.vec + size_t(id1 - g.global_offset) * dpad);
+        float d0, d1;
+        if constexpr (kRegQ) {
+          qr.dist2(r0, r1, a0, a1, nchunks, s, d0, d1);
+        } else {
+          d0 = dist_smemq<METRIC>(sm.query, r0, a0, nchunks, s);
+          d1 = dist_smemq<METRIC>(sm.query, r1, a1, nchunks, s);
+        }
+        if (s == 0) {
+          if (a0) sm.cand_keys[i0] = make_key(d0, id0);
+          if (a1) sm.cand_keys[i1] = make_key(d1, id1);
+        }
+      }
+      __syncwarp();
+      uint64_t v0 = lane < m ? sm.cand_keys[lane] : kKeyMax;
+      uint64_t v1 = lane + 32 < m ? sm.cand_keys[lane + 32] : kKeyMax;
+      warp_sort64(v0, v1, lane);
+      sm.cand_keys[lane] = v0;
+      sm.cand_keys[lane + 32] = v1;
+      __syncwarp();
+    };
+
+    // Seed the beam with the medoid (beam_search.cuh:114-123).
+    uint64_t* cur = sm.beam0;
+    uint64_t* nxt = sm.beam1;
+    if (lane == 0) {
+      sm.cand_ids[0] = g.medoid;
+      hash_insert(sm.hash, HBITS, g.medoid);
+    }
+    __syncwarp();
+    evaluate_and_sort(1);
+    if (lane == 0) cur[0] = sm.cand_keys[0];
+    uint32_t cnt = 1;
+    uint32_t n_hash = 1;
+    uint32_t expansions = 0, deg_sum = 0, evals = 1, resets = 0;
+    __syncwarp();
+
+    uint32_t loop_count = 0;
+    while (loop_count <= a.limit) {
+      loop_count++;
+      // choose_new_frontier: first unvisited entry of the sorted beam.
+      int pos = -1;
+      for (uint32_t base = 0; base < cnt; base += 32) {
+        const uint32_t i = base + lane;
+        const bool unv = i < cnt && !key_visited(cur[i]);
+        const uint32_t bal = __ballot_sync(kFull, unv);
+        if (bal) { pos = int(base) + __ffs(bal) - 1; break; }
+      }
+      if (pos < 0) break;
+      const uint64_t fkey = cur[pos];
+      __syncwarp();
+      if (lane == 0) cur[pos] = fkey | 1ull;
+      const uint32_t u = key_id(fkey);
+      if (a.vis_idx != nullptr && lane == 0) {
+        a.vis_idx[size_t(q) * a.max_result_size + expansions] = u;
+        a.vis_dist[size_t(q) * a.max_result_size + expansions] = key_dist(fkey);
+      }
+      expansions++;
+      if (expansions == a.max_result_size) break;
+
+      // Keep the visited-distance table at most half full: clear it and refill
+      // it with the beam, so beam members are always recognised.
+      if (n_hash + R > hsize / 2) {
+        __syncwarp();
+        for (uint32_t i = lane; i < hsize; i += 32) sm.hash[i] = kHashEmpty;
+        __syncwarp();
+        for (uint32_t i = lane; i < cnt; i += 32) hash_insert(sm.hash, HBITS, key_id(cur[i]));
+        n_hash = cnt;
+        resets++;
+        __syncwarp();
+      }
+
+      // add_frontier_out: the neighbour list of u, in-range ids not seen before.
+      const uint32_t lu = u - g.global_offset;
+      const uint32_t ne = g.counts[lu];
+      deg_sum += ne;
+      const uint32_t* el = g.edges + size_t(lu) * R;
+      uint32_t nb0 = lane < ne ? __ldg(el + lane) : kInvalid;
+      uint32_t nb1 = lane + 32 < ne ? __ldg(el + lane + 32) : kInvalid;
+      bool f0 = (lane < ne) && (nb0 - g.global_offset < g.n) && hash_insert(sm.hash, HBITS, nb0);
+      const uint32_t b0 = __ballot_sync(kFull, f0);
+      bool f1 = (lane + 32 < ne) && (nb1 - g.global_offset < g.n) && hash_insert(sm.hash, HBITS, nb1);
+      const uint32_t b1 = __ballot_sync(kFull, f1);
+      const uint32_t lt = (1u << lane) - 1u;
+      if (f0) sm.cand_ids[__popc(b0 & lt)] = nb0;
+      if (f1) sm.cand_ids[__popc(b0) + __popc(b1 & lt)] = nb1;
+      const int m = __popc(b0) + __popc(b1);
+      n_hash += m;
+      __syncwarp();
+      if (m == 0) continue;
+      evals += m;
+      evaluate_and_sort(m);
+
+      // Merge beam (cnt) and candidates (m) by rank; keep the first bw.
+      for (uint32_t i = lane; i < cnt; i += 32) {
+        const uint64_t b = cur[i];
+        const uint32_t p = i + lower_rank(sm.cand_keys, m, b);
+        if (p < bw) nxt[p] = b;
+      }
+      for (int j = lane; j < m; j += 32) {
+        const uint64_t c = sm.cand_keys[j];
+        const uint32_t p = j + lower_rank(cur, int(cnt), c);
+        if (p < bw) nxt[p] = c;
+      }
+      cnt = min(bw, cnt + uint32_t(m));
+      uint64_t* t = cur; cur = nxt; nxt = t;
+      __syncwarp();
+    }
+
+    // Output the first k non-deleted entries (beam_search.cuh:205-222).
+    if (a.out_idx != nullptr) {
+      uint32_t out = 0;
+      for (uint32_t base = 0; base < cnt && out < a.k; base += 32) {
+        const uint32_t i = base + lane;
+        uint32_t id = 0;
+        bool ok = false;
+        if (i < cnt) {
+          id = key_id(cur[i]);
+          const uint32_t l = id - g.global_offset;
+          ok = !(g.deleted != nullptr && ((g.deleted[l >> 5] >> (l & 31)) & 1u));
+        }
+        const uint32_t bal = __ballot_sync(kFull, ok);
+        const uint32_t p = out + __popc(bal & ((1u << lane) - 1u));
+        if (ok && p < a.k) {
+          const uint32_t sid = g.ids_identity ? id : g.slot_to_id[id - g.global_offset];
+          a.out_idx[size_t(q) * a.k + p] = int32_t(sid);
+          a.out_dist[size_t(q) * a.k + p] = key_dist(cur[i]);
+        }
+        out += __popc(bal);
+      }
+      for (uint32_t p = out + lane; p < a.k; p += 32) {
+        a.out_idx[size_t(q) * a.k + p] = -1;
+        a.out_dist[size_t(q) * a.k + p] = 1e30f;
+      }
+    }
+    if (lane == 0) {
+      if (a.vis_cnt != nullptr) a.vis_cnt[q] = expansions;
+      if (a.stats != nullptr) {
+        a.stats[size_t(q) * 4 + 0] = expansions;
+        a.stats[size_t(q) * 4 + 1] = deg_sum;
+        a.stats[size_t(q) * 4 + 2] = evals;
+        a.stats[size_t(q) * 4 + 3] = resets;
+      }
+    }
+    __syncwarp();
+  }
+}
+
+template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC>
+void launch_t(const SearchArgs& a, cudaStream_t stream) {
+  auto kern = beam_search_warp_kernel<BWCAP, HBITS, MAXC, METRIC>;
+  const size_t per_warp = warp_smem_bytes(BWCAP, HBITS, a.g.dpad, MAXC == 0);
+  int wpb = 4;
+  while (wpb > 1 && per_warp * wpb > 200 * 1024) wpb--;
+  if (per_warp * wpb > 220 * 1024) throw std::runtime_error("search: shared memory per query too large");
+  const size_t smem = per_warp * wpb;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  int dev = 0, sms = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * wpb, smem);
+  if (per_sm < 1) per_sm = 1;
+  const uint32_t need = (a.nq + wpb - 1) / wpb;
+  uint32_t grid = uint32_t(sms) * uint32_t(per_sm);
+  if (grid > need) grid = need;
+  if (grid == 0) return;
+  kern<<<grid, 32 * wpb, smem, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("search launch: ") + cudaGetErrorString(e));
+}
+
+template <uint32_t BWCAP, uint32_t HBITS>
+void dispatch_dim(const SearchArgs& a, cudaStream_t stream) {
+  const uint32_t nchunks = a.g.dpad / 8;
+  if (a.g.metric == kIP) return launch_t<BWCAP, HBITS, 0, kIP>(a, stream);
+  if (nchunks <= 4) return launch_t<BWCAP, HBITS, 1, kL2>(a, stream);
+  if (nchunks <= 8) return launch_t<BWCAP, HBITS, 2, kL2>(a, stream);
+  if (nchunks <= 12) return launch_t<BWCAP, HBITS, 3, kL2>(a, stream);
+  if (nchunks <= 16) return launch_t<BWCAP, HBITS, 4, kL2>(a, stream);
+  if (nchunks <= 32) return launch_t<BWCAP, HBITS, 8, kL2>(a, stream);
+  return launch_t<BWCAP, HBITS, 0, kL2>(a, stream);
+}
+
+}  // namespace
+
+void launch_search(const SearchArgs& a, cudaStream_t stream) {
+  if (a.nq == 0) return;
+  if (a.g.R > 64) throw std::runtime_error("search: R > 64 is not supported");
+  if (a.bw == 0) throw std::runtime_error("search: beam_width must be > 0");
+  // Same bound as the reference's width dispatch (beam_search/api.cuh:64-72).
+  if (a.bw + 64 >= 2048)
+    throw std::invalid_argument("beam_width " + std::to_string(a.bw) +
+                                " is too large (beam_width + 64 must be < 2048)");
+  if (a.bw <= 64) return dispatch_dim<64, 11>(a, stream);
+  if (a.bw <= 128) return dispatch_dim<128, 11>(a, stream);
+  if (a.bw <= 256) return dispatch_dim<256, 11>(a, stream);
+  if (a.bw <= 512) return dispatch_dim<512, 12>(a, stream);
+  return dispatch_dim<2048, 14>(a, stream);
+}
+
+}  // namespace jb

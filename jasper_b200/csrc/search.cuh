@@ -1,0 +1,39 @@
+// search.cuh -- launch interface of the warp-per-query beam search.
+#pragma once
+#include <cuda_runtime.h>
+#include "jb_graph.h"
+
+namespace jb {
+
+struct SearchArgs {
+  GraphView g;
+  // Query rows: either `queries` ([nq][g.dpad] fp16, 16-byte aligned rows) or,
+  // when use_range, graph rows [query_start, query_start + nq) (the build).
+  const uint16_t* queries;
+  int use_range;
+  uint32_t query_start;
+  uint32_t nq;
+  uint32_t k;
+  uint32_t bw;
+  uint32_t limit;
+  uint32_t max_result_size;
+  int32_t* out_idx;   // [nq][k] or null
+  float* out_dist;    // [nq][k] or null
+  uint32_t* vis_idx;  // [nq][max_result_size] expansion order, or null
+  float* vis_dist;
+  uint32_t* vis_cnt;  // [nq]
+  uint32_t* work_counter;  // one zeroed uint32 per launch (dynamic query scheduling)
+  uint32_t* stats;         // optional [nq][4]: expansions, sum of degrees, distance evals, hash resets
+};
+
+// Bytes of device scratch a search launch needs (the work counter).
+constexpr size_t kSearchScratchBytes = 256;
+
+// Enqueue the search on `stream`.  `work_counter` must point at zeroed device
+// memory (the caller clears it on the same stream).  Throws on bad arguments.
+void launch_search(const SearchArgs& a, cudaStream_t stream);
+
+// Number of kernel launches launch_search issues (for launch accounting).
+constexpr int kSearchLaunches = 1;
+
+}  // namespace jb

@@ -1,0 +1,176 @@
+"""ctypes wrapper of the CPU restatement (jasper_oracle.c).
+
+TEST INFRASTRUCTURE ONLY.  tests/, __graft_entry__.smoke() and the
+cpu_baseline leg of bench.py use it as the checker; the jasper_b200 product
+never imports it.  Build with ``make -C oracle`` (or __graft_entry__.build()).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libjasper_oracle.so"
+
+
+class _Graph(C.Structure):
+    _fields_ = [
+        ("n", C.c_uint32), ("dim", C.c_uint32), ("dpad", C.c_uint32), ("R", C.c_uint32),
+        ("metric", C.c_int), ("medoid", C.c_uint32), ("global_offset", C.c_uint32),
+        ("vec", C.c_void_p), ("edges", C.c_void_p), ("edist", C.c_void_p),
+        ("counts", C.c_void_p), ("deleted", C.c_void_p),
+    ]
+
+
+_lib = None
+
+
+def build() -> Path:
+    src = HERE / "jasper_oracle.c"
+    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = C.CDLL(str(LIB_PATH))
+        P = C.c_void_p
+        L.orc_distance_f32.argtypes = [C.c_int, P, P, C.c_int]
+        L.orc_distance_f32.restype = C.c_float
+        L.orc_distance_f16.argtypes = [C.c_int, P, P, C.c_int]
+        L.orc_distance_f16.restype = C.c_float
+        L.orc_half_to_float.argtypes = [C.c_uint16]
+        L.orc_half_to_float.restype = C.c_float
+        L.orc_float_to_bf16.argtypes = [C.c_float]
+        L.orc_float_to_bf16.restype = C.c_uint16
+        L.orc_search.argtypes = [C.POINTER(_Graph), P, C.c_uint32, C.c_uint32, C.c_uint32,
+                                 C.c_uint32, C.c_uint32, P, P, P, P]
+        L.orc_search.restype = None
+        L.orc_search_one.argtypes = [C.POINTER(_Graph), P, C.c_uint32, C.c_uint32, C.c_uint32,
+                                     C.c_uint32, P, P, P, P, P]
+        L.orc_search_one.restype = C.c_uint32
+        L.orc_build.argtypes = [C.POINTER(_Graph), C.c_float, C.c_uint32]
+        L.orc_build.restype = None
+        L.orc_bruteforce.argtypes = [P, C.c_uint32, P, C.c_uint32, C.c_uint32, C.c_int,
+                                     C.c_uint32, P, P]
+        L.orc_bruteforce.restype = None
+        L.orc_set_threads.argtypes = [C.c_int]
+        L.orc_set_threads.restype = None
+        L.orc_max_threads.argtypes = []
+        L.orc_max_threads.restype = C.c_int
+        _lib = L
+    return _lib
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(int(n))
+
+
+def max_threads() -> int:
+    return int(lib().orc_max_threads())
+
+
+def _p(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def pad_rows(x: np.ndarray) -> np.ndarray:
+    """fp16 [n, dim] -> uint16 bit patterns [n, dpad] with zero pad lanes."""
+    x = np.ascontiguousarray(x, dtype=np.float16)
+    n, d = x.shape
+    dpad = (d + 7) // 8 * 8
+    out = np.zeros((n, dpad), dtype=np.uint16)
+    out[:, :d] = x.view(np.uint16)
+    return out
+
+
+class OracleGraph:
+    """A graph in the oracle's flat layout (numpy arrays, CPU)."""
+
+    def __init__(self, vectors: np.ndarray, R: int, metric: int = 0, medoid: int = 0,
+                 global_offset: int = 0):
+        v = np.ascontiguousarray(vectors, dtype=np.float16)
+        self.n, self.dim = v.shape
+        self.vec = pad_rows(v)
+        self.dpad = self.vec.shape[1]
+        self.R = R
+        self.metric = metric
+        self.medoid = medoid
+        self.global_offset = global_offset
+        self.edges = np.full((self.n, R), 0xFFFFFFFF, dtype=np.uint32)
+        self.edist = np.zeros((self.n, R), dtype=np.uint16)
+        self.counts = np.zeros(self.n, dtype=np.uint8)
+        self.deleted: np.ndarray | None = None
+
+    def _struct(self) -> _Graph:
+        return _Graph(self.n, self.dim, self.dpad, self.R, self.metric, self.medoid,
+                      self.global_offset, _p(self.vec), _p(self.edges), _p(self.edist),
+                      _p(self.counts), _p(self.deleted))
+
+    def build(self, alpha: float, max_batch_size: int) -> None:
+        g = self._struct()
+        lib().orc_build(C.byref(g), float(alpha), int(max_batch_size))
+
+    def search(self, queries: np.ndarray, k: int, beam_width: int, limit: int,
+               max_result_size: int = 2048):
+        q = pad_rows(queries)
+        assert q.shape[1] == self.dpad
+        nq = q.shape[0]
+        oi = np.zeros((nq, k), dtype=np.uint32)
+        od = np.zeros((nq, k), dtype=np.float32)
+        ne = np.zeros(nq, dtype=np.uint32)
+        ev = np.zeros(nq, dtype=np.uint64)
+        g = self._struct()
+        lib().orc_search(C.byref(g), _p(q), nq, k, beam_width, limit, max_result_size,
+                         _p(oi), _p(od), _p(ne), _p(ev))
+        return oi.view(np.int32), od, ne, ev
+
+    def search_visited(self, query: np.ndarray, k: int, beam_width: int, limit: int,
+                       max_result_size: int):
+        """One query with its expansion order (the build's search)."""
+        q = pad_rows(query.reshape(1, -1))
+        oi = np.zeros(k, dtype=np.uint32)
+        od = np.zeros(k, dtype=np.float32)
+        vi = np.zeros(max_result_size, dtype=np.uint32)
+        vd = np.zeros(max_result_size, dtype=np.float32)
+        g = self._struct()
+        n = lib().orc_search_one(C.byref(g), _p(q), k, beam_width, limit, max_result_size,
+                                 _p(oi), _p(od), _p(vi), _p(vd), None)
+        return oi.view(np.int32), od, vi[:n].view(np.int32), vd[:n]
+
+
+def distance_f32(metric: int, a, b, dim: int) -> float:
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    return float(lib().orc_distance_f32(metric, _p(a), _p(b), dim))
+
+
+def distance_f16(metric: int, a, b, dim: int | None = None) -> float:
+    a = pad_rows(np.asarray(a, dtype=np.float16).reshape(1, -1))[0]
+    b = pad_rows(np.asarray(b, dtype=np.float16).reshape(1, -1))[0]
+    return float(lib().orc_distance_f16(metric, _p(a), _p(b), a.shape[0] if dim is None else dim))
+
+
+def bruteforce(base: np.ndarray, queries: np.ndarray, k: int, metric: int = 0):
+    b = pad_rows(base)
+    q = pad_rows(queries)
+    nq = q.shape[0]
+    oi = np.zeros((nq, k), dtype=np.uint32)
+    od = np.zeros((nq, k), dtype=np.float32)
+    lib().orc_bruteforce(_p(b), b.shape[0], _p(q), nq, b.shape[1], metric, k, _p(oi), _p(od))
+    return oi.view(np.int32), od
+
+
+def reference_max_batch_size(budget_bytes: int, n: int, R: int) -> int:
+    """graph_construct_workspace::max_batch_size_for_budget (construct.cuh:233-258)
+    capped at n / 50 (ffi/jasper_ffi_common.cuh:245-248)."""
+    L, mrs = 64, 256
+    per_item = 8 * L + 8 * mrs + 4 + 8 * (mrs + R) + 4 + 8 * R + 4 * R + 4 * R
+    b = 0 if budget_bytes <= 4 else (budget_bytes - 4) // per_item
+    return min(b, n // 50)

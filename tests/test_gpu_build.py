@@ -1,0 +1,84 @@
+"""Build parity: jasper_b200's batched construction against the CPU
+restatement, and both against graphs built by the reference's CUDA code.
+
+The construction is deterministic in both implementations (same batch ramp,
+same search, same (distance, id) candidate order, same RobustPrune), so the
+adjacency must match exactly: ids, bf16 edge distances and counts.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from jasper_b200 import synthetic
+from oracle import oracle as O
+import jb_testlib as T
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+CASES = [
+    # kind, n, dim, R, metric, alpha
+    ("gaussian", 3000, 128, 32, 0, 1.2),
+    ("sift_like", 3000, 128, 64, 0, 1.2),
+    ("gaussian", 2500, 96, 16, 0, 1.2),
+    ("gaussian", 2000, 128, 32, 1, 1.0),
+    ("gaussian", 1200, 40, 8, 0, 1.2),
+    ("gaussian", 30, 16, 8, 0, 1.2),     # n < 50: one row per batch
+    ("relu_sphere", 1500, 320, 32, 1, 1.0),
+]
+
+
+def assert_graph_equal(e, d, c, g, msg=""):
+    np.testing.assert_array_equal(c, g.counts, err_msg=msg)
+    for i in range(g.n):
+        k = int(c[i])
+        np.testing.assert_array_equal(e[i, :k], g.edges[i, :k], err_msg=f"{msg} row {i}")
+        np.testing.assert_array_equal(d[i, :k], g.edist[i, :k], err_msg=f"{msg} row {i}")
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"{c[0]}-n{c[1]}-d{c[2]}-R{c[3]}-m{c[4]}")
+def test_build_matches_oracle(cuda, case):
+    kind, n, dim, R, metric, alpha = case
+    X = getattr(synthetic, kind)(n, dim, 31)
+    budget = 10 * 10**9
+    g = O.OracleGraph(X, R, metric=metric)
+    g.build(alpha, max(1, O.reference_max_batch_size(budget, n, R)))
+    h = T.construct(X, R, metric, alpha, budget)
+    try:
+        e, d, c = T.get_edges(h, n, R)
+        assert_graph_equal(e, d, c, g, msg=str(case))
+    finally:
+        T.free(h)
+
+
+def golden_cases():
+    return sorted(GOLDEN.glob("*.npz"))
+
+
+@pytest.mark.parametrize("path", golden_cases(), ids=lambda p: p.stem)
+def test_golden_build_and_search_match_reference(cuda, path):
+    from test_oracle import regen
+    z = np.load(path)
+    X, Q = regen(z)
+    R = int(z["R"])
+    metric = 0 if str(z["metric"]) == "l2" else 1
+    h = T.construct(X, R, metric, float(z["alpha"]))
+    try:
+        e, d, c = T.get_edges(h, int(z["n"]), R)
+        ref = O.OracleGraph(X, R, metric=metric, medoid=int(z["medoid"]))
+        ref.edges[:] = z["edges"]
+        ref.edist[:] = z["dists"]
+        ref.counts[:] = z["counts"]
+        assert_graph_equal(e, d, c, ref, msg=path.stem)
+    finally:
+        T.free(h)
+    # search on the reference's own graph
+    h = T.create_graph(ref)
+    try:
+        for bw in z["bws"]:
+            bw = int(bw)
+            ji, jd = T.search(h, Q, 10, bw)
+            T.assert_same_results(ji, jd, z[f"idx_bw{bw}"], z[f"dist_bw{bw}"], msg=f"bw={bw}")
+    finally:
+        T.free(h)
