@@ -88,12 +88,16 @@ int jb_graph_search(int64_t handle, const uint16_t* queries, uint64_t n_queries,
                     uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
                     uint32_t beam_width, uint32_t limit, void* stream);
 
-/* Same search with per-query counters: stats[q][0..3] = expansions, sum of
- * expanded degrees, distance evaluations, visited-table resets (device
- * pointer, [n_queries][4] uint32).  Asynchronous. */
+/* Same search with per-query counters (instrumentation): stats[q][0..4] =
+ * expansions, sum of expanded degrees, distance evaluations, visited-table
+ * resets, distinct rows evaluated (device pointer, [n_queries][5] uint32).
+ * The last needs `seen_scratch`: zeroed device memory of
+ * n_queries * ceil(n_vectors / 32) uint32 words (else it repeats field 2).
+ * Asynchronous. */
 int jb_graph_search_stats(int64_t handle, const uint16_t* queries, uint64_t n_queries,
                           uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
-                          uint32_t beam_width, uint32_t limit, uint32_t* stats, void* stream);
+                          uint32_t beam_width, uint32_t limit, uint32_t* stats,
+                          uint32_t* seen_scratch, void* stream);
 
 /* End-to-end search from host buffers: copies the queries in, searches and
  * copies the results back.  Synchronous (the reference's Search_ also

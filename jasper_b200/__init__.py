@@ -244,18 +244,25 @@ class Graph:
         return out_i, out_d
 
     def search_with_stats(self, queries: torch.Tensor, k: int = 10, beam_width: int = 64,
-                          limit: int | None = None):
-        """search() plus per-query counters [nq, 4] (expansions, expanded degree
-        sum, distance evaluations, visited-table resets)."""
+                          limit: int | None = None, distinct: bool = False):
+        """search() plus per-query counters [nq, 5]: expansions, expanded degree
+        sum, distance evaluations, visited-table resets, distinct rows
+        evaluated (exact only with ``distinct=True``, which needs
+        nq * n_vectors / 8 bytes of scratch)."""
         self._check_alive()
         queries = self._check_queries(queries)
         nq = queries.size(0)
         out_i = torch.empty(nq, k, dtype=torch.int32, device=queries.device)
         out_d = torch.empty(nq, k, dtype=torch.float32, device=queries.device)
-        stats = torch.zeros(nq, 4, dtype=torch.int32, device=queries.device)
+        stats = torch.zeros(nq, 5, dtype=torch.int32, device=queries.device)
+        seen = None
+        if distinct:
+            words = (self.n_vectors + 31) // 32
+            seen = torch.zeros(nq * words, dtype=torch.int32, device=queries.device)
         limit = beam_width * 2 if limit is None else limit
         _lib.call("jb_graph_search_stats", self._handle, _ptr(queries), nq, self._dim, _ptr(out_i),
-                  _ptr(out_d), k, beam_width, limit, _ptr(stats), _stream_ptr(queries.device))
+                  _ptr(out_d), k, beam_width, limit, _ptr(stats),
+                  None if seen is None else _ptr(seen), _stream_ptr(queries.device))
         return out_i, out_d, stats
 
     def directional_search(self, queries: torch.Tensor, k: int = 10, beam_width: int = 64,

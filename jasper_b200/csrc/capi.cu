@@ -103,7 +103,7 @@ void check_metric(int32_t metric) {
 // the padded dim are first packed into a padded scratch copy.
 void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint32_t row_stride,
                  int32_t* out_idx, float* out_dist, uint32_t k, uint32_t bw, uint32_t limit,
-                 uint32_t* stats, cudaStream_t st) {
+                 uint32_t* stats, uint32_t* seen, cudaStream_t st) {
   if (nq == 0) return;
   if (nq > 0x7FFFFFFFull) throw std::invalid_argument("too many queries");
   if (k == 0) throw std::invalid_argument("k must be > 0");
@@ -136,6 +136,7 @@ void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint3
   a.out_dist = out_dist;
   a.work_counter = static_cast<uint32_t*>(counter);
   a.stats = stats;
+  a.seen_bits = seen;
   try {
     jb::launch_search(a, st);
   } catch (...) {
@@ -227,18 +228,19 @@ int jb_graph_search(int64_t handle, const uint16_t* queries, uint64_t n_queries,
     auto g = lookup(handle);
     DeviceScope ds(g->device);
     search_impl(*g, queries, n_queries, row_stride, out_idx, out_dist, k, beam_width, limit,
-                nullptr, static_cast<cudaStream_t>(stream));
+                nullptr, nullptr, static_cast<cudaStream_t>(stream));
   });
 }
 
 int jb_graph_search_stats(int64_t handle, const uint16_t* queries, uint64_t n_queries,
                           uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
-                          uint32_t beam_width, uint32_t limit, uint32_t* stats, void* stream) {
+                          uint32_t beam_width, uint32_t limit, uint32_t* stats,
+                          uint32_t* seen_scratch, void* stream) {
   return guarded([&] {
     auto g = lookup(handle);
     DeviceScope ds(g->device);
     search_impl(*g, queries, n_queries, row_stride, out_idx, out_dist, k, beam_width, limit, stats,
-                static_cast<cudaStream_t>(stream));
+                seen_scratch, static_cast<cudaStream_t>(stream));
   });
 }
 
@@ -266,7 +268,7 @@ int jb_graph_search_host(int64_t handle, const uint16_t* queries, uint64_t n_que
                    "copy queries");
       }
       search_impl(*g, static_cast<uint16_t*>(dq), n_queries, g->dpad, static_cast<int32_t*>(di),
-                  static_cast<float*>(dd), k, beam_width, limit, nullptr, st);
+                  static_cast<float*>(dd), k, beam_width, limit, nullptr, nullptr, st);
       cuda_check(cudaMemcpyAsync(out_idx, di, obytes, cudaMemcpyDeviceToHost, st), "copy idx");
       cuda_check(cudaMemcpyAsync(out_dist, dd, obytes, cudaMemcpyDeviceToHost, st), "copy dist");
     } catch (...) {

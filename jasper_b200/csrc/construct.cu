@@ -26,10 +26,12 @@
 // Every phase is stream-ordered with no host round trip, so a whole build is
 // a sequence of asynchronous launches.
 //
-// One deliberate difference: when a target collects more than 256 + R
-// candidates in (e), the reference keeps whichever ones its shared-memory
-// atomics place first; this code keeps the 256 + R best by (distance, id).
-// Below that cap (the common case) the two are identical.
+// Candidate cap in (e): at most 256 + R candidates per target
+// (construct.cuh:574).  When a target has more, the reference keeps whichever
+// ones its shared-memory atomics place first -- in practice the existing edges
+// (one cheap pass) and then the sinks in group order.  This code keeps exactly
+// that, deterministically: existing edges, then sinks in (target, sink) order
+// until the cap; the sinks past the cap are never evaluated.
 #include <cub/device/device_radix_sort.cuh>
 #include <stdexcept>
 #include <string>
@@ -290,12 +292,9 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
       end += __ffs(~bal) - 1;
       break;
     }
-    // Sinks with fresh distances, 16 per pass (two rows per 4-lane tile).
-    for (size_t i = start; i < end; i += 16) {
-      if (nc + 16 > int(kMaxCandSort)) {  // keep the `cap` best so far
-        sort_cands(sm.cand, nc, lane);
-        if (nc > int(cap)) nc = int(cap);
-      }
+    // Sinks with fresh distances, 16 per pass (two rows per 4-lane tile), in
+    // group order, until the candidate cap.
+    for (size_t i = start; i < end && nc < int(cap); i += 16) {
       const size_t i0 = i + tile, i1 = i + tile + 8;
       const uint32_t s0 = i0 < end ? uint32_t(keys[i0]) : kInvalid;
       const uint32_t s1 = i1 < end ? uint32_t(keys[i1]) : kInvalid;
@@ -307,15 +306,16 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
       const uint32_t b1 = __ballot_sync(kFull, a1 && s == 0);
       if (s == 0) {
         const uint32_t lt = (1u << lane) - 1u;
-        if (a0) sm.cand[nc + __popc(b0 & lt)] = make_pair_key(d0, s0);
-        if (a1) sm.cand[nc + __popc(b0) + __popc(b1 & lt)] = make_pair_key(d1, s1);
+        const int p0 = nc + __popc(b0 & lt);
+        const int p1 = nc + __popc(b0) + __popc(b1 & lt);
+        if (a0 && p0 < int(cap)) sm.cand[p0] = make_pair_key(d0, s0);
+        if (a1 && p1 < int(cap)) sm.cand[p1] = make_pair_key(d1, s1);
       }
-      nc += __popc(b0) + __popc(b1);
+      nc = min(int(cap), nc + __popc(b0) + __popc(b1));
       __syncwarp();
     }
     __syncwarp();
     sort_cands(sm.cand, nc, lane);
-    if (nc > int(cap)) nc = int(cap);
     prune_and_write<MAXC, METRIC>(g, t, sm, nc, alpha, lane);
   }
 }

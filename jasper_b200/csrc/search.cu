@@ -192,6 +192,7 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
     for (uint32_t i = lane; i < hsize; i += 32) sm.hash[i] = kHashEmpty;
     __syncwarp();
 
+    uint32_t first_evals = 0;  // per lane; summed at the end (stats only)
     // Evaluate candidates sm.cand_ids[0, m) into sm.cand_keys (sorted on exit).
     auto evaluate_and_sort = [&](int m) {
       for (int base = 0; base < m; base += 16) {
@@ -211,6 +212,12 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
         if (s == 0) {
           if (a0) sm.cand_keys[i0] = make_key(d0, id0);
           if (a1) sm.cand_keys[i1] = make_key(d1, id1);
+          if (a.seen_bits != nullptr) {
+            uint32_t* bits = a.seen_bits + size_t(q) * ((g.n + 31) / 32);
+            const uint32_t l0 = id0 - g.global_offset, l1 = id1 - g.global_offset;
+            if (a0 && !(atomicOr(&bits[l0 >> 5], 1u << (l0 & 31)) & (1u << (l0 & 31)))) first_evals++;
+            if (a1 && !(atomicOr(&bits[l1 >> 5], 1u << (l1 & 31)) & (1u << (l1 & 31)))) first_evals++;
+          }
         }
       }
       __syncwarp();
@@ -335,13 +342,18 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
         a.out_dist[size_t(q) * a.k + p] = 1e30f;
       }
     }
+    if (a.stats != nullptr) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) first_evals += __shfl_xor_sync(kFull, first_evals, o);
+    }
     if (lane == 0) {
       if (a.vis_cnt != nullptr) a.vis_cnt[q] = expansions;
       if (a.stats != nullptr) {
-        a.stats[size_t(q) * 4 + 0] = expansions;
-        a.stats[size_t(q) * 4 + 1] = deg_sum;
-        a.stats[size_t(q) * 4 + 2] = evals;
-        a.stats[size_t(q) * 4 + 3] = resets;
+        a.stats[size_t(q) * 5 + 0] = expansions;
+        a.stats[size_t(q) * 5 + 1] = deg_sum;
+        a.stats[size_t(q) * 5 + 2] = evals;
+        a.stats[size_t(q) * 5 + 3] = resets;
+        a.stats[size_t(q) * 5 + 4] = a.seen_bits != nullptr ? first_evals : evals;
       }
     }
     __syncwarp();

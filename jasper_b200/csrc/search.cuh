@@ -23,7 +23,10 @@ struct SearchArgs {
   float* vis_dist;
   uint32_t* vis_cnt;  // [nq]
   uint32_t* work_counter;  // one zeroed uint32 per launch (dynamic query scheduling)
-  uint32_t* stats;         // optional [nq][4]: expansions, sum of degrees, distance evals, hash resets
+  uint32_t* stats;         // optional [nq][5]: expansions, sum of degrees, distance evals,
+                           // visited-table resets, first-time distance evals
+  uint32_t* seen_bits;     // optional zeroed [nq][ceil(n / 32)] bitmap; with it stats[4]
+                           // counts each distinct row once (the roofline's numerator)
 };
 
 // Bytes of device scratch a search launch needs (the work counter).

@@ -435,10 +435,13 @@ static void batch_prune_body(void *vctx, long b) {
 }
 
 /* (e) process_reverse_edges_kernel (construct.cuh:560-741) for one target.
- * When the candidates exceed MAX_CANDS = 256 + R the reference keeps
- * whichever slots its shared-memory atomics hand out first; this restatement
- * keeps the MAX_CANDS best by (distance, id), the deterministic choice
- * jasper_b200 also makes.  Below the cap both are identical. */
+ * Candidates are the target's existing edges (stored bf16 distances) and the
+ * reverse sinks with fresh distances, at most MAX_CANDS = 256 + R of them.
+ * When there are more, the reference keeps whichever ones its shared-memory
+ * atomics place first, which is the existing edges (one cheap pass) and then
+ * the sinks roughly in group order; this restatement keeps exactly that: the
+ * existing edges, then sinks in (target, sink) order until the cap.  Below the
+ * cap both are identical. */
 static void batch_reverse_body(void *vctx, long gi) {
   batch_ctx *c = (batch_ctx *)vctx;
   orc_graph *g = c->g;
@@ -446,35 +449,25 @@ static void batch_reverse_body(void *vctx, long gi) {
   uint32_t t = c->rev[c->gstart[gi]].src;
   size_t nr = c->gstart[gi + 1] - c->gstart[gi];
   size_t l = t - g->global_offset;
-  orc_pair *cand = (orc_pair *)malloc(sizeof(orc_pair) * (R + nr));
+  orc_pair *cand = (orc_pair *)malloc(sizeof(orc_pair) * maxc);
   uint32_t nc = 0;
   for (uint32_t i = 0; i < g->counts[l]; i++) {
     uint32_t nb = g->edges[l * R + i];
     if (nb == ORC_INVALID) continue;
     cand[nc].id = nb; cand[nc].d = orc_bf16_to_float(g->edist[l * R + i]); nc++;
   }
-  for (size_t i = 0; i < nr; i++) {
+  for (size_t i = 0; i < nr && nc < maxc; i++) {
     uint32_t s = c->rev[c->gstart[gi] + i].sink;
     if (s == ORC_INVALID || s == t) continue;
     cand[nc].id = s;
     cand[nc].d = orc_distance_f16(g->metric, row(g, t), row(g, s), (int)g->dim);
     nc++;
   }
-  /* keep the best maxc in sorted order (bounded insertion) */
-  orc_pair *best = (orc_pair *)malloc(sizeof(orc_pair) * maxc);
-  uint32_t nb = 0;
-  for (uint32_t i = 0; i < nc; i++) {
-    if (nb == maxc && !pair_less(&cand[i], &best[nb - 1])) continue;
-    int j = (int)(nb < maxc ? nb : maxc - 1) - 1;
-    if (nb < maxc) nb++;
-    while (j >= 0 && pair_less(&cand[i], &best[j])) { best[j + 1] = best[j]; j--; }
-    best[j + 1] = cand[i];
-  }
+  sort_pairs(cand, (int)nc);
   uint32_t sel[256];
   float sel_d[256];
-  uint32_t ns = robust_prune(g, t, best, nb, c->alpha, sel, sel_d);
+  uint32_t ns = robust_prune(g, t, cand, nc, c->alpha, sel, sel_d);
   write_row(g, t, sel, sel_d, ns);
-  free(best);
   free(cand);
 }
 

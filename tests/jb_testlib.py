@@ -36,9 +36,12 @@ def search(h: int, Q: np.ndarray, k: int, bw: int, limit: int | None = None, sta
     limit = 2 * bw if limit is None else limit
     st = torch.cuda.current_stream().cuda_stream
     if stats:
-        s = torch.zeros(nq, 4, dtype=torch.int32, device="cuda")
+        s = torch.zeros(nq, 5, dtype=torch.int32, device="cuda")
+        info = _lib.GraphInfo()
+        _lib.call("jb_graph_get_info", h, C.byref(info))
+        seen = torch.zeros(nq * ((info.n_vectors + 31) // 32), dtype=torch.int32, device="cuda")
         _lib.call("jb_graph_search_stats", h, q.data_ptr(), nq, q.shape[1], oi.data_ptr(),
-                  od.data_ptr(), k, bw, limit, s.data_ptr(), st)
+                  od.data_ptr(), k, bw, limit, s.data_ptr(), seen.data_ptr(), st)
         torch.cuda.synchronize()
         return oi.cpu().numpy(), od.cpu().numpy(), s.cpu().numpy()
     _lib.call("jb_graph_search", h, q.data_ptr(), nq, q.shape[1], oi.data_ptr(), od.data_ptr(),

@@ -26,6 +26,8 @@ CASES = [
     ("gaussian", 1200, 40, 8, 0, 1.2),
     ("gaussian", 30, 16, 8, 0, 1.2),     # n < 50: one row per batch
     ("relu_sphere", 1500, 320, 32, 1, 1.0),
+    # batches of 400 rows: hub targets collect more than 256 + R candidates
+    ("sift_like", 20000, 128, 64, 0, 1.2),
 ]
 
 
