@@ -62,7 +62,40 @@ def build(verbose: bool = False) -> Path:
             raise RuntimeError("link failed:\n" + r.stderr)
         if verbose:
             print("built", so)
+    _build_tvm_module(so, verbose)
     return so
+
+
+def _tvm_include() -> Path | None:
+    try:
+        import tvm_ffi
+    except ImportError:
+        return None
+    inc = Path(tvm_ffi.__file__).resolve().parent / "include"
+    return inc if inc.exists() else None
+
+
+def _build_tvm_module(core: Path, verbose: bool) -> Path | None:
+    """lib/libjasper_ffi.so: the reference's tvm_ffi op names over the C ABI."""
+    inc = _tvm_include()
+    if inc is None:
+        return None
+    tvm_lib = inc.parent / "lib"
+    src = CSRC / "ffi_tvm.cc"
+    out = LIB / "libjasper_ffi.so"
+    if out.exists() and out.stat().st_mtime > max(src.stat().st_mtime, core.stat().st_mtime,
+                                                    _headers_mtime()):
+        return out
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-o", str(out), str(src),
+           f"-I{inc}", f"-I{ROOT / 'include'}", "-I/usr/local/cuda/include",
+           f"-L{LIB}", "-ljasper_b200", f"-L{tvm_lib}", "-ltvm_ffi",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{tvm_lib}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("tvm_ffi module build failed:\n" + r.stderr)
+    if verbose:
+        print("built", out)
+    return out
 
 
 if __name__ == "__main__":
