@@ -106,6 +106,23 @@ int jb_graph_search_host(int64_t handle, const uint16_t* queries, uint64_t n_que
                          uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
                          uint32_t beam_width, uint32_t limit, void* stream);
 
+/* Search without any device allocation.  No counterpart in the reference.
+ * For callers that cannot allocate device memory while they search: code
+ * that runs under a fixed, pre-reserved memory budget, code whose process
+ * owns an allocator this library must not bypass, or code that may not touch
+ * the CUDA allocator while other work is in flight.  Same arguments and
+ * results as jb_graph_search (device pointers, asynchronous on `stream`).
+ * Its scratch is a fixed 4 MiB device array inside this library, held on
+ * every GPU that loads it until the process exits: the work counter, plus a
+ * repacked copy of the queries when their rows are not at stride
+ * ceil(dim/8)*8 with a 16-byte aligned base; a call that would need more than
+ * that is rejected with JB_ERR_INVALID_ARGUMENT.  All calls share the array,
+ * so calls that overlap on the GPU race.  The first call on each device looks
+ * up the array's device address: make it before any stream capture. */
+int jb_graph_search_noalloc(int64_t handle, const uint16_t* queries, uint64_t n_queries,
+                            uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
+                            uint32_t beam_width, uint32_t limit, void* stream);
+
 /* Release a graph (reference: FreeGraph, ffi/jasper_ffi_plain.cu:15-47). */
 int jb_graph_free(int64_t handle);
 

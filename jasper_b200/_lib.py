@@ -45,6 +45,7 @@ SIGNATURES: dict[str, list] = {
     "jb_graph_search": [_I64, _P, _U64, _U32, _P, _P, _U32, _U32, _U32, _P],
     "jb_graph_search_stats": [_I64, _P, _U64, _U32, _P, _P, _U32, _U32, _U32, _P, _P, _P],
     "jb_graph_search_host": [_I64, _P, _U64, _U32, _P, _P, _U32, _U32, _U32, _P],
+    "jb_graph_search_noalloc": [_I64, _P, _U64, _U32, _P, _P, _U32, _U32, _U32, _P],
     "jb_graph_free": [_I64],
     "jb_graph_get_info": [_I64, C.POINTER(GraphInfo)],
     "jb_graph_get_vector": [_I64, _I64, _P],

@@ -5,6 +5,7 @@
 // held only for lookups; the op bodies run unlocked.
 #include <cuda_runtime.h>
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <mutex>
 #include <stdexcept>
@@ -149,6 +150,13 @@ void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint3
 }
 
 }  // namespace
+
+// Handle lookup and error reporting for entry points defined in other files
+// of this library (noalloc.cu).
+namespace jb {
+std::shared_ptr<Graph> capi_lookup(int64_t h) { return lookup(h); }
+int capi_guarded(const std::function<void()>& f) { return guarded(f); }
+}  // namespace jb
 
 extern "C" {
 
