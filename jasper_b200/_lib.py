@@ -6,9 +6,11 @@ loudly when it is missing: there is no CPU fallback for any operation.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "lib" / "libjasper_b200.so"
+LIB_PATH = Path(os.environ.get("JASPER_B200_LIB") or
+                Path(__file__).resolve().parent / "lib" / "libjasper_b200.so")
 
 JB_OK = 0
 JB_ERR_INVALID_ARGUMENT = 1

@@ -120,6 +120,21 @@ __device__ __forceinline__ void warp_sort64(uint64_t& v0, uint64_t& v1, int lane
   }
 }
 
+// Warp-wide bitonic sort of 32 keys, one per lane (ascending by lane).
+__device__ __forceinline__ uint64_t warp_sort32(uint64_t v, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      uint64_t o = __shfl_xor_sync(kFull, v, j);
+      const bool up = (lane & k) == 0;
+      const bool low = (lane & j) == 0;
+      v = (low == up) ? (v < o ? v : o) : (v < o ? o : v);
+    }
+  }
+  return v;
+}
+
 // Bitonic sort of n (power of two, <= 32 * 32) keys in shared memory by one warp.
 __device__ __forceinline__ void warp_sort_smem(uint64_t* a, int n, int lane) {
   for (int k = 2; k <= n; k <<= 1) {

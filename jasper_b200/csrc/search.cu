@@ -44,6 +44,20 @@ namespace {
 
 constexpr uint32_t kHashEmpty = 0xFFFFFFFFu;
 
+// Optional per-phase cycle counters (build with -DJB_PHASE_CLOCKS; read with
+// jb_debug_phase_clocks): 0 init, 1 choose, 2 neighbour list + filter,
+// 3 distances, 4 candidate sort, 5 merge, 6 table reset, 7 output.
+#ifdef JB_PHASE_CLOCKS
+__device__ unsigned long long g_phase_clocks[8];
+#define JB_CLK_DECL unsigned long long _clk_acc[8] = {0, 0, 0, 0, 0, 0, 0, 0}; long long _clk_t = clock64();
+#define JB_CLK(p) { long long _n = clock64(); _clk_acc[p] += _n - _clk_t; _clk_t = _n; }
+#define JB_CLK_FLUSH if (lane == 0) { for (int _i = 0; _i < 8; _i++) atomicAdd(&g_phase_clocks[_i], _clk_acc[_i]); }
+#else
+#define JB_CLK_DECL
+#define JB_CLK(p)
+#define JB_CLK_FLUSH
+#endif
+
 struct WarpSmem {
   uint64_t* beam0;
   uint64_t* beam1;
@@ -51,19 +65,25 @@ struct WarpSmem {
   uint32_t* cand_ids;   // [64]
   uint32_t* hash;       // [1 << hbits]
   uint16_t* query;      // [dpad] (shared-memory query path only)
+  float2* qpairs;       // [dpad / 2] query pairs (lane-per-row path)
 };
 
 __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
 
+// nq: chunk quads of the lane-per-row instance (template MAXC), 0 for the
+// shared-memory-query instance.
 __host__ __device__ inline size_t warp_smem_bytes(uint32_t bwcap, uint32_t hbits, uint32_t dpad,
-                                                  bool smem_query) {
+                                                  uint32_t nq) {
+  const bool smem_query = nq == 0;
   size_t b = 0;
   b += 2 * sizeof(uint64_t) * bwcap;
   b += sizeof(uint64_t) * 64;
   b += sizeof(uint32_t) * 64;
   b += sizeof(uint32_t) * (size_t(1) << hbits);
   b = align16(b);
+  // lane-per-row query pairs: 2 * nq chunk pairs x 8 float2
   if (smem_query) b += align16(sizeof(uint16_t) * dpad);
+  else b += size_t(128) * nq;
   return b;
 }
 
@@ -76,6 +96,7 @@ __device__ __forceinline__ WarpSmem carve(char* base, uint32_t bwcap, uint32_t h
   s.hash = s.cand_ids + 64;
   size_t off = align16(reinterpret_cast<char*>(s.hash + (size_t(1) << hbits)) - base);
   s.query = reinterpret_cast<uint16_t*>(base + off);
+  s.qpairs = reinterpret_cast<float2*>(base + off);
   return s;
 }
 
@@ -92,42 +113,6 @@ __device__ __forceinline__ bool hash_insert(uint32_t* h, uint32_t hbits, uint32_
   }
   return true;
 }
-
-// Distance of one query to rows of the graph, per 4-lane tile.
-// REG: query chunks in registers (L2, dpad <= 32 * MAXC * 8 / 4).
-template <int MAXC, int METRIC>
-struct QueryReg {
-  uint4 q[MAXC];
-  __device__ __forceinline__ void load(const uint4* row, int nchunks, int s) {
-#pragma unroll
-    for (int i = 0; i < MAXC; i++) {
-      int c = s + 4 * i;
-      q[i] = c < nchunks ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
-    }
-  }
-  // Distances of two rows at once (r1 may alias r0).  Returns tile-reduced sums.
-  __device__ __forceinline__ void dist2(const uint4* r0, const uint4* r1, bool a0, bool a1,
-                                        int nchunks, int s, float& d0, float& d1) const {
-    uint4 x[MAXC], y[MAXC];
-#pragma unroll
-    for (int i = 0; i < MAXC; i++) {
-      int c = s + 4 * i;
-      x[i] = (a0 && c < nchunks) ? ldg16(r0 + c) : make_uint4(0, 0, 0, 0);
-      y[i] = (a1 && c < nchunks) ? ldg16(r1 + c) : make_uint4(0, 0, 0, 0);
-    }
-    float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll
-    for (int i = 0; i < MAXC; i++) {
-      int c = s + 4 * i;
-      if (c < nchunks) {
-        acc0 = l2_chunk(q[i], x[i], acc0);
-        acc1 = l2_chunk(q[i], y[i], acc1);
-      }
-    }
-    d0 = tile4_sum(acc0);
-    d1 = tile4_sum(acc1);
-  }
-};
 
 // Shared-memory query: any dpad, L2 or inner product.
 template <int METRIC>
@@ -156,14 +141,119 @@ __device__ __forceinline__ float dist_smemq(const uint16_t* qs, const uint4* row
   return METRIC == kL2 ? acc : -acc;
 }
 
+// ── lane-per-row distances (dpad <= 256) ───────────────────────────────────
+// One lane computes a whole candidate row, reproducing the reference's four
+// per-lane partial sums as two packed f32x2 chains: (s0, s1) and (s2, s3).
+// L2: partial t walks 16-byte chunks t, t+4, ... with one fma per element, so
+// chunks (4i, 4i+1) feed the pair (s0, s1) and (4i+2, 4i+3) feed (s2, s3),
+// element by element; the query is kept negated, (x - q)^2 == (q - x)^2.
+// Inner product: partial t walks elements t, t+4, ... of every chunk, so the
+// half2 words (e0, e1), (e4, e5) feed (s0, s1) and (e2, e3), (e6, e7) feed
+// (s2, s3) in that order.  Both end with (s0 + s2) + (s1 + s3), the
+// reference's 4-lane butterfly.  L2 rows missing a chunk read zeros, which
+// add nothing (fma(0, 0, acc) == acc for the non-negative partials).
+//
+// qpairs layout -- L2: qpairs[p * 8 + e] = (-q[2p][e], -q[2p + 1][e]) for
+// chunk pairs p < 2 * NQ (zeros past the row); IP: qpairs[c * 4 + w] =
+// (q[c][2w], q[c][2w + 1]) for c < nchunks <= 4 * NQ.  Both fit the 128 * NQ
+// bytes warp_smem_bytes reserves for the instance.
+template <int NQ, int METRIC>
+__device__ __forceinline__ void build_qpairs(float2* qp, const uint16_t* qrow, int nchunks, int lane) {
+  const __half* qh = reinterpret_cast<const __half*>(qrow);
+  if (METRIC == kL2) {
+    // every pair row_dist_lane<NQ> reads: 2 per chunk quad, zeros past the row
+    const int npairs = 2 * NQ;
+    for (int t = lane; t < npairs * 8; t += 32) {
+      const int p = t >> 3, e = t & 7;
+      const int c0 = 2 * p, c1 = 2 * p + 1;
+      const float a = c0 < nchunks ? __half2float(qh[c0 * 8 + e]) : 0.f;
+      const float b = c1 < nchunks ? __half2float(qh[c1 * 8 + e]) : 0.f;
+      qp[t] = make_float2(-a, -b);
+    }
+  } else {
+    for (int t = lane; t < nchunks * 4; t += 32)
+      qp[t] = make_float2(__half2float(qh[2 * t]), __half2float(qh[2 * t + 1]));
+  }
+}
+
+__device__ __forceinline__ float2 h2f(uint32_t w) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+
+template <int NQ, int METRIC>
+__device__ __forceinline__ float row_dist_lane(const float2* qp, const uint4* row, int nchunks) {
+  float2 acc01 = make_float2(0.f, 0.f), acc23 = make_float2(0.f, 0.f);
+  constexpr int G = NQ < 4 ? NQ : 4;  // chunk quads per load group (4 * G loads in flight)
+  if (METRIC == kL2) {
+#pragma unroll
+    for (int g0 = 0; g0 < NQ; g0 += G) {
+      uint4 u[4 * G];
+#pragma unroll
+      for (int k = 0; k < 4 * G; k++) {
+        const int c = 4 * g0 + k;
+        u[k] = c < nchunks ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int qi = 0; qi < G; qi++) {
+        const int i = g0 + qi;
+#pragma unroll
+        for (int half = 0; half < 2; half++) {
+          const uint4 ua = u[4 * qi + 2 * half], ub = u[4 * qi + 2 * half + 1];
+          const float2* qq = qp + (2 * i + half) * 8;
+          float2& acc = half ? acc23 : acc01;
+          const uint32_t aw[4] = {ua.x, ua.y, ua.z, ua.w};
+          const uint32_t bw[4] = {ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+          for (int w = 0; w < 4; w++) {
+            const float2 fa = h2f(aw[w]), fb = h2f(bw[w]);
+            const float4 q2 = *reinterpret_cast<const float4*>(qq + 2 * w);
+            float2 d0 = __fadd2_rn(make_float2(fa.x, fb.x), make_float2(q2.x, q2.y));
+            acc = __ffma2_rn(d0, d0, acc);
+            float2 d1 = __fadd2_rn(make_float2(fa.y, fb.y), make_float2(q2.z, q2.w));
+            acc = __ffma2_rn(d1, d1, acc);
+          }
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int g0 = 0; g0 < 4 * NQ; g0 += 4 * G) {
+      uint4 u[4 * G];
+#pragma unroll
+      for (int k = 0; k < 4 * G; k++) {
+        const int c = g0 + k;
+        u[k] = c < nchunks ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int k = 0; k < 4 * G; k++) {
+        const int c = g0 + k;
+        if (c < nchunks) {
+          const float4 qa = *reinterpret_cast<const float4*>(qp + c * 4);
+          const float4 qb = *reinterpret_cast<const float4*>(qp + c * 4 + 2);
+          acc01 = __ffma2_rn(h2f(u[k].x), make_float2(qa.x, qa.y), acc01);
+          acc23 = __ffma2_rn(h2f(u[k].y), make_float2(qa.z, qa.w), acc23);
+          acc01 = __ffma2_rn(h2f(u[k].z), make_float2(qb.x, qb.y), acc01);
+          acc23 = __ffma2_rn(h2f(u[k].w), make_float2(qb.z, qb.w), acc23);
+        }
+      }
+    }
+  }
+  const float2 sum = __fadd2_rn(acc01, acc23);
+  const float r = __fadd_rn(sum.x, sum.y);
+  return METRIC == kL2 ? r : -r;
+}
+
+#ifndef JB_SEARCH_MIN_BLOCKS
+#define JB_SEARCH_MIN_BLOCKS 4
+#endif
 template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC>
-__global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
+__global__ void __launch_bounds__(128, JB_SEARCH_MIN_BLOCKS) beam_search_warp_kernel(SearchArgs a) {
   constexpr bool kRegQ = (MAXC > 0);
   extern __shared__ __align__(16) char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int wid = threadIdx.x >> 5;
   const uint32_t dpad = a.g.dpad;
-  const size_t per_warp = warp_smem_bytes(BWCAP, HBITS, dpad, !kRegQ);
+  const size_t per_warp = warp_smem_bytes(BWCAP, HBITS, dpad, MAXC);
   WarpSmem sm = carve(smem_raw + per_warp * wid, BWCAP, HBITS);
   const int tile = lane >> 2, s = lane & 3;
   const int nchunks = int(dpad / 8);
@@ -172,6 +262,7 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
   const uint32_t R = g.R;
   const uint32_t bw = a.bw;
 
+  JB_CLK_DECL
   for (;;) {
     uint32_t q = 0;
     if (lane == 0) q = atomicAdd(a.work_counter, 1u);
@@ -181,9 +272,9 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
     const uint16_t* qrow = a.use_range
         ? g.vec + size_t(a.query_start + q - g.global_offset) * dpad
         : a.queries + size_t(q) * dpad;
-    QueryReg<(MAXC > 0 ? MAXC : 1), METRIC> qr;
     if constexpr (kRegQ) {
-      qr.load(reinterpret_cast<const uint4*>(qrow), nchunks, s);
+      build_qpairs<MAXC, METRIC>(sm.qpairs, qrow, nchunks, lane);
+      __syncwarp();
     } else {
       const uint4* src = reinterpret_cast<const uint4*>(qrow);
       uint4* dst = reinterpret_cast<uint4*>(sm.query);
@@ -194,7 +285,31 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
 
     uint32_t first_evals = 0;  // per lane; summed at the end (stats only)
     // Evaluate candidates sm.cand_ids[0, m) into sm.cand_keys (sorted on exit).
-    auto evaluate_and_sort = [&](int m) {
+    uint64_t* cur = sm.beam0;
+    uint64_t* nxt = sm.beam1;
+    uint32_t cnt = 0;
+    // Evaluates sm.cand_ids[0, m), then keeps only candidates that can enter
+    // the beam -- with the beam full, a key above its bw-th entry would land
+    // past position bw in the merged order and be clipped -- and leaves them
+    // sorted in sm.cand_keys.  Returns how many were kept.
+    auto evaluate_and_sort = [&](int m) -> int {
+      if constexpr (kRegQ) {
+        // One lane per candidate row (32 rows per pass).
+        for (int base = 0; base < m; base += 32) {
+          const int j = base + lane;
+          if (j < m) {
+            const uint32_t id = sm.cand_ids[j];
+            const uint4* row = reinterpret_cast<const uint4*>(g.vec + size_t(id - g.global_offset) * dpad);
+            const float d = row_dist_lane<MAXC, METRIC>(sm.qpairs, row, nchunks);
+            sm.cand_keys[j] = make_key(d, id);
+            if (a.seen_bits != nullptr) {
+              uint32_t* bits = a.seen_bits + size_t(q) * ((g.n + 31) / 32);
+              const uint32_t l = id - g.global_offset;
+              if (!(atomicOr(&bits[l >> 5], 1u << (l & 31)) & (1u << (l & 31)))) first_evals++;
+            }
+          }
+        }
+      } else
       for (int base = 0; base < m; base += 16) {
         const int i0 = base + tile, i1 = base + tile + 8;
         const bool a0 = i0 < m, a1 = i1 < m;
@@ -202,13 +317,8 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
         const uint32_t id1 = a1 ? sm.cand_ids[i1] : id0;
         const uint4* r0 = reinterpret_cast<const uint4*>(g.vec + size_t(id0 - g.global_offset) * dpad);
         const uint4* r1 = reinterpret_cast<const uint4*>(g.vec + size_t(id1 - g.global_offset) * dpad);
-        float d0, d1;
-        if constexpr (kRegQ) {
-          qr.dist2(r0, r1, a0, a1, nchunks, s, d0, d1);
-        } else {
-          d0 = dist_smemq<METRIC>(sm.query, r0, a0, nchunks, s);
-          d1 = dist_smemq<METRIC>(sm.query, r1, a1, nchunks, s);
-        }
+        const float d0 = dist_smemq<METRIC>(sm.query, r0, a0, nchunks, s);
+        const float d1 = dist_smemq<METRIC>(sm.query, r1, a1, nchunks, s);
         if (s == 0) {
           if (a0) sm.cand_keys[i0] = make_key(d0, id0);
           if (a1) sm.cand_keys[i1] = make_key(d1, id1);
@@ -221,17 +331,37 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
         }
       }
       __syncwarp();
+      JB_CLK(3)
       uint64_t v0 = lane < m ? sm.cand_keys[lane] : kKeyMax;
       uint64_t v1 = lane + 32 < m ? sm.cand_keys[lane + 32] : kKeyMax;
-      warp_sort64(v0, v1, lane);
-      sm.cand_keys[lane] = v0;
-      sm.cand_keys[lane + 32] = v1;
+      if (cnt == bw) {
+        const uint64_t worst = cur[bw - 1] | 1ull;  // ids differ: the flag bit never decides
+        if (v0 > worst) v0 = kKeyMax;
+        if (v1 > worst) v1 = kKeyMax;
+      }
+      const uint32_t k0 = __ballot_sync(kFull, v0 != kKeyMax);
+      const uint32_t k1 = __ballot_sync(kFull, v1 != kKeyMax);
+      const int kept = __popc(k0) + __popc(k1);
       __syncwarp();
+      if (kept <= 32) {  // the common case: compact to one key per lane
+        const uint32_t lt = (1u << lane) - 1u;
+        if (v0 != kKeyMax) sm.cand_keys[__popc(k0 & lt)] = v0;
+        if (v1 != kKeyMax) sm.cand_keys[__popc(k0) + __popc(k1 & lt)] = v1;
+        __syncwarp();
+        uint64_t v = lane < kept ? sm.cand_keys[lane] : kKeyMax;
+        v = warp_sort32(v, lane);
+        sm.cand_keys[lane] = v;
+      } else {
+        warp_sort64(v0, v1, lane);
+        sm.cand_keys[lane] = v0;
+        sm.cand_keys[lane + 32] = v1;
+      }
+      __syncwarp();
+      JB_CLK(4)
+      return kept;
     };
 
     // Seed the beam with the medoid (beam_search.cuh:114-123).
-    uint64_t* cur = sm.beam0;
-    uint64_t* nxt = sm.beam1;
     if (lane == 0) {
       sm.cand_ids[0] = g.medoid;
       hash_insert(sm.hash, HBITS, g.medoid);
@@ -239,12 +369,13 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
     __syncwarp();
     evaluate_and_sort(1);
     if (lane == 0) cur[0] = sm.cand_keys[0];
-    uint32_t cnt = 1;
+    cnt = 1;
     uint32_t n_hash = 1;
     uint32_t expansions = 0, deg_sum = 0, evals = 1, resets = 0;
     __syncwarp();
 
     uint32_t loop_count = 0;
+    JB_CLK(0)
     while (loop_count <= a.limit) {
       loop_count++;
       // choose_new_frontier: first unvisited entry of the sorted beam.
@@ -255,6 +386,7 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
         const uint32_t bal = __ballot_sync(kFull, unv);
         if (bal) { pos = int(base) + __ffs(bal) - 1; break; }
       }
+      JB_CLK(1)
       if (pos < 0) break;
       const uint64_t fkey = cur[pos];
       __syncwarp();
@@ -278,14 +410,17 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
         resets++;
         __syncwarp();
       }
+      JB_CLK(6)
 
       // add_frontier_out: the neighbour list of u, in-range ids not seen before.
       const uint32_t lu = u - g.global_offset;
       const uint32_t ne = g.counts[lu];
       deg_sum += ne;
       const uint32_t* el = g.edges + size_t(lu) * R;
-      uint32_t nb0 = lane < ne ? __ldg(el + lane) : kInvalid;
-      uint32_t nb1 = lane + 32 < ne ? __ldg(el + lane + 32) : kInvalid;
+      // Issued together with the count load (slots past the count are masked
+      // below), so the two dependent gathers overlap.
+      uint32_t nb0 = lane < R ? __ldg(el + lane) : kInvalid;
+      uint32_t nb1 = lane + 32 < R ? __ldg(el + lane + 32) : kInvalid;
       bool f0 = (lane < ne) && (nb0 - g.global_offset < g.n) && hash_insert(sm.hash, HBITS, nb0);
       const uint32_t b0 = __ballot_sync(kFull, f0);
       bool f1 = (lane + 32 < ne) && (nb1 - g.global_offset < g.n) && hash_insert(sm.hash, HBITS, nb1);
@@ -296,26 +431,30 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
       const int m = __popc(b0) + __popc(b1);
       n_hash += m;
       __syncwarp();
+      JB_CLK(2)
       if (m == 0) continue;
       evals += m;
-      evaluate_and_sort(m);
+      const int kept = evaluate_and_sort(m);
+      if (kept == 0) continue;
 
-      // Merge beam (cnt) and candidates (m) by rank; keep the first bw.
+      // Merge beam (cnt) and kept candidates by rank; keep the first bw.
       for (uint32_t i = lane; i < cnt; i += 32) {
         const uint64_t b = cur[i];
-        const uint32_t p = i + lower_rank(sm.cand_keys, m, b);
+        const uint32_t p = i + lower_rank(sm.cand_keys, kept, b);
         if (p < bw) nxt[p] = b;
       }
-      for (int j = lane; j < m; j += 32) {
+      for (int j = lane; j < kept; j += 32) {
         const uint64_t c = sm.cand_keys[j];
         const uint32_t p = j + lower_rank(cur, int(cnt), c);
         if (p < bw) nxt[p] = c;
       }
-      cnt = min(bw, cnt + uint32_t(m));
+      cnt = min(bw, cnt + uint32_t(kept));
       uint64_t* t = cur; cur = nxt; nxt = t;
       __syncwarp();
+      JB_CLK(5)
     }
 
+    JB_CLK(1)
     // Output the first k non-deleted entries (beam_search.cuh:205-222).
     if (a.out_idx != nullptr) {
       uint32_t out = 0;
@@ -357,13 +496,15 @@ __global__ void __launch_bounds__(128) beam_search_warp_kernel(SearchArgs a) {
       }
     }
     __syncwarp();
+    JB_CLK(7)
   }
+  JB_CLK_FLUSH
 }
 
 template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC>
 void launch_t(const SearchArgs& a, cudaStream_t stream) {
   auto kern = beam_search_warp_kernel<BWCAP, HBITS, MAXC, METRIC>;
-  const size_t per_warp = warp_smem_bytes(BWCAP, HBITS, a.g.dpad, MAXC == 0);
+  const size_t per_warp = warp_smem_bytes(BWCAP, HBITS, a.g.dpad, MAXC);
   int wpb = 4;
   while (wpb > 1 && per_warp * wpb > 200 * 1024) wpb--;
   if (per_warp * wpb > 220 * 1024) throw std::runtime_error("search: shared memory per query too large");
@@ -386,7 +527,14 @@ void launch_t(const SearchArgs& a, cudaStream_t stream) {
 template <uint32_t BWCAP, uint32_t HBITS>
 void dispatch_dim(const SearchArgs& a, cudaStream_t stream) {
   const uint32_t nchunks = a.g.dpad / 8;
-  if (a.g.metric == kIP) return launch_t<BWCAP, HBITS, 0, kIP>(a, stream);
+  if (a.g.metric == kIP) {
+    if (nchunks <= 4) return launch_t<BWCAP, HBITS, 1, kIP>(a, stream);
+    if (nchunks <= 8) return launch_t<BWCAP, HBITS, 2, kIP>(a, stream);
+    if (nchunks <= 12) return launch_t<BWCAP, HBITS, 3, kIP>(a, stream);
+    if (nchunks <= 16) return launch_t<BWCAP, HBITS, 4, kIP>(a, stream);
+    if (nchunks <= 32) return launch_t<BWCAP, HBITS, 8, kIP>(a, stream);
+    return launch_t<BWCAP, HBITS, 0, kIP>(a, stream);
+  }
   if (nchunks <= 4) return launch_t<BWCAP, HBITS, 1, kL2>(a, stream);
   if (nchunks <= 8) return launch_t<BWCAP, HBITS, 2, kL2>(a, stream);
   if (nchunks <= 12) return launch_t<BWCAP, HBITS, 3, kL2>(a, stream);
@@ -396,6 +544,17 @@ void dispatch_dim(const SearchArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+#ifdef JB_PHASE_CLOCKS
+extern "C" int jb_debug_phase_clocks(unsigned long long* out, int reset) {
+  if (cudaMemcpyFromSymbol(out, g_phase_clocks, sizeof(unsigned long long) * 8) != cudaSuccess) return 1;
+  if (reset) {
+    unsigned long long z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    cudaMemcpyToSymbol(g_phase_clocks, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
 
 void launch_search(const SearchArgs& a, cudaStream_t stream) {
   if (a.nq == 0) return;
