@@ -76,6 +76,70 @@ struct RowReg {
       qs = smem_row;
     }
   }
+  // Kept-row cache (L2, register path): kept row j lives at sel + j * stride
+  // (stride = dpad / 8 chunks); with swz its chunk c sits at c ^ 4 on odd
+  // rows, so tiles 2p and 2p+1 (rows j, j+1) read disjoint bank groups.
+  __device__ __forceinline__ static int sel_slot(int j, int c, int stride, bool swz) {
+    return j * stride + (swz ? (c ^ ((j & 1) << 2)) : c);
+  }
+  __device__ __forceinline__ void store_sel(uint4* sel, int j, int nchunks, int stride, bool swz,
+                                            int s) const {
+    if constexpr (MAXC > 0) {
+#pragma unroll
+      for (int i = 0; i < MAXC; i++) {
+        const int c = s + 4 * i;
+        if (c < nchunks) sel[sel_slot(j, c, stride, swz)] = q[i];
+      }
+    }
+  }
+  __device__ __forceinline__ float dist_sel(const uint4* sel, int j, bool active, int nchunks,
+                                            int stride, bool swz, int s) const {
+    float acc = 0.f;
+    if constexpr (MAXC > 0) {
+#pragma unroll
+      for (int i = 0; i < MAXC; i++) {
+        const int c = s + 4 * i;
+        if (c < nchunks) {
+          const uint4 x = active ? sel[sel_slot(j, c, stride, swz)] : make_uint4(0, 0, 0, 0);
+          acc = l2_chunk(q[i], x, acc);
+        }
+      }
+    }
+    return tile4_sum(acc);
+  }
+  // dist() from global memory for one tile on its own path.
+  __device__ __forceinline__ float dist_local(const GraphView& g, uint32_t id, int nchunks,
+                                              int lane) const {
+    const uint4* row = reinterpret_cast<const uint4*>(g.vec + size_t(id - g.global_offset) * g.dpad);
+    const int s = lane & 3;
+    float acc = 0.f;
+    if constexpr (MAXC > 0) {
+      uint4 x[MAXC];
+#pragma unroll
+      for (int i = 0; i < MAXC; i++) {
+        const int c = s + 4 * i;
+        x[i] = c < nchunks ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int i = 0; i < MAXC; i++)
+        if (s + 4 * i < nchunks) acc = l2_chunk(q[i], x[i], acc);
+    }
+    return tile4_sum_local(acc, lane);
+  }
+  // dist_sel for one tile on its own path (tile-local reduction).
+  __device__ __forceinline__ float dist_sel_local(const uint4* sel, int j, int nchunks,
+                                                  int stride, bool swz, int lane) const {
+    float acc = 0.f;
+    const int s = lane & 3;
+    if constexpr (MAXC > 0) {
+#pragma unroll
+      for (int i = 0; i < MAXC; i++) {
+        const int c = s + 4 * i;
+        if (c < nchunks) acc = l2_chunk(q[i], sel[sel_slot(j, c, stride, swz)], acc);
+      }
+    }
+    return tile4_sum_local(acc, lane);
+  }
   __device__ __forceinline__ float dist(const GraphView& g, uint32_t id, bool active,
                                         int nchunks, int s) const {
     const uint4* row = reinterpret_cast<const uint4*>(g.vec + size_t(id - g.global_offset) * g.dpad);
@@ -118,18 +182,43 @@ struct PruneSmem {
   uint32_t* sel;    // [64]
   float* sel_d;     // [64]
   uint16_t* row;    // [dpad] (shared-memory row path)
+  uint4* selrows;   // [64][dpad / 8] kept rows (L2 register path only)
+};
+constexpr int kPruneGroup = 8;
+
+// RobustPrune strategy: 0 one candidate at a time, kept rows re-read from
+// global memory; 1 groups of 8 candidates, kept rows from global memory;
+// 2 groups of 8, kept rows cached in shared memory.
+#ifndef JB_PRUNE_MODE
+#define JB_PRUNE_MODE 1
+#endif
+
+#ifdef JB_BUILD_CLOCKS
+__device__ unsigned long long g_build_clk[4];
+#endif  // candidates tested at once, one per 4-lane tile
+
+// The kept-row cache is used where the candidate row sits in registers (L2,
+// dpad <= 256): every prune test then reads the kept row from shared memory.
+template <int MAXC, int METRIC>
+struct SelCache {
+  static constexpr bool on = JB_PRUNE_MODE == 2 && MAXC > 0 && METRIC == kL2;
+  static constexpr bool batch = JB_PRUNE_MODE >= 1 && MAXC > 0 && METRIC == kL2;
 };
 
-__host__ __device__ inline size_t prune_warp_bytes(uint32_t dpad) {
-  return kMaxCandSort * 8 + 64 * 4 + 64 * 4 + ((size_t(dpad) * 2 + 15) & ~size_t(15));
+__host__ __device__ inline size_t prune_warp_bytes(uint32_t dpad, bool sel_cache) {
+  size_t b = kMaxCandSort * 8 + 64 * 4 + 64 * 4 + ((size_t(dpad) * 2 + 15) & ~size_t(15));
+  if (sel_cache) b += size_t(64) * dpad * 2;
+  return b;
 }
 
-__device__ __forceinline__ PruneSmem prune_carve(char* base) {
+__device__ __forceinline__ PruneSmem prune_carve(char* base, uint32_t dpad) {
   PruneSmem p;
   p.cand = reinterpret_cast<uint64_t*>(base);
   p.sel = reinterpret_cast<uint32_t*>(p.cand + kMaxCandSort);
   p.sel_d = reinterpret_cast<float*>(p.sel + 64);
   p.row = reinterpret_cast<uint16_t*>(p.sel_d + 64);
+  p.selrows = reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.row) +
+                                       ((size_t(dpad) * 2 + 15) & ~size_t(15)));
   return p;
 }
 
@@ -144,13 +233,79 @@ __device__ __forceinline__ void sort_cands(uint64_t* cand, int nc, int lane) {
 
 // RobustPrune over sorted candidate pair keys; writes the row of `self`.
 template <int MAXC, int METRIC>
-__device__ void prune_and_write(const GraphView& g, uint32_t self, PruneSmem& sm, int nc,
+__device__ void prune_and_write(const GraphView& gv, uint32_t self, PruneSmem& sm, int nc,
                                 float alpha, int lane) {
+  const GraphView& g = gv;
   const int tile = lane >> 2, s = lane & 3;
   const int nchunks = int(g.dim / 8);
   const uint32_t R = g.R;
   uint32_t ns = 0;
   RowReg<MAXC, METRIC> cr;
+  constexpr bool kSel = SelCache<MAXC, METRIC>::on;
+  constexpr bool kBatch = SelCache<MAXC, METRIC>::batch;
+  const int stride = int(g.dpad / 8);
+  const bool swz = (stride & 7) == 0;
+  if constexpr (kBatch) {
+    // Groups of up to 8 candidates in list order, one per 4-lane tile.
+    // Phase 1: each tile tests its candidate against the kept set as it was
+    // when the group started (its own early exit).  Phase 2, in list order:
+    // a survivor is accepted unless a row accepted earlier in this group
+    // prunes it.  Pruning only grows with the kept set, so this accepts
+    // exactly what the one-at-a-time loop accepts.
+    const int tile = lane >> 2;
+    int i = 0;
+    while (i < nc && ns < R) {
+      const int w = i + lane;
+      const uint64_t wk = w < nc ? sm.cand[w] : kKeyMax;
+      const bool valid = w < nc && pair_id(wk) != self && pair_id(wk) != kInvalid;
+      const uint32_t bal = __ballot_sync(kFull, valid);
+      const int nvalid = __popc(bal);
+      if (nvalid == 0) { i += 32; continue; }
+      const int gsz = nvalid < kPruneGroup ? nvalid : kPruneGroup;
+      // position of the tile-th valid candidate in the window
+      uint32_t rem = bal;
+      for (int t = 0; t < tile && rem; t++) rem &= rem - 1;
+      const bool mine = tile < gsz;
+      const int pos = mine ? i + __ffs(rem) - 1 : i;
+      int last = i;  // window position of the g-th valid candidate
+      {
+        uint32_t r2 = bal;
+        for (int t = 0; t < gsz - 1; t++) r2 &= r2 - 1;
+        last = i + __ffs(r2) - 1;
+      }
+      const uint64_t key = sm.cand[pos];
+      const uint32_t cid = pair_id(key);
+      const float cd = key_dist(key);
+      if (mine) cr.load(gv, cid, nchunks, lane, sm.row);
+      bool pruned = !mine;
+      if (mine) {
+        for (uint32_t j = 0; j < ns; j++) {
+          const float d = kSel ? cr.dist_sel_local(sm.selrows, int(j), nchunks, stride, swz, lane)
+                               : cr.dist_local(g, sm.sel[j], nchunks, lane);
+          if (d * alpha < cd) { pruned = true; break; }
+        }
+      }
+      __syncwarp();
+      for (int t = 0; t < gsz; t++) {
+        if (ns >= R) break;
+        const bool tp = __shfl_sync(kFull, pruned ? 1 : 0, t * 4) != 0;
+        if (tp) continue;
+        const float tcd = __shfl_sync(kFull, cd, t * 4);
+        const uint32_t tid = __shfl_sync(kFull, cid, t * 4);
+        if (lane == 0) { sm.sel[ns] = tid; sm.sel_d[ns] = tcd; }
+        if (kSel && tile == t) cr.store_sel(sm.selrows, int(ns), nchunks, stride, swz, lane & 3);
+        __syncwarp();
+        // later survivors of the group against the row just accepted
+        const bool act = tile > t && !pruned;
+        const float d = kSel ? cr.dist_sel(sm.selrows, int(ns), act, nchunks, stride, swz, lane & 3)
+                             : cr.dist(g, act ? tid : cid, act, nchunks, lane & 3);
+        if (tile > t && !pruned && d * alpha < cd) pruned = true;
+        ns++;
+        __syncwarp();
+      }
+      i = last + 1;
+    }
+  } else
   for (int i = 0; i < nc; i++) {
     if (ns >= R) break;
     const uint64_t key = sm.cand[i];
@@ -162,13 +317,22 @@ __device__ void prune_and_write(const GraphView& g, uint32_t self, PruneSmem& sm
     for (uint32_t base = 0; base < ns; base += 16) {
       const uint32_t j0 = base + tile, j1 = base + tile + 8;
       const bool a0 = j0 < ns, a1 = j1 < ns;
-      const float d0 = cr.dist(g, a0 ? sm.sel[j0] : cid, a0, nchunks, s);
-      const float d1 = cr.dist(g, a1 ? sm.sel[j1] : cid, a1, nchunks, s);
+      float d0, d1;
+      if constexpr (kSel) {
+        d0 = cr.dist_sel(sm.selrows, int(j0), a0, nchunks, stride, swz, s);
+        d1 = cr.dist_sel(sm.selrows, int(j1), a1, nchunks, stride, swz, s);
+      } else {
+        d0 = cr.dist(g, a0 ? sm.sel[j0] : cid, a0, nchunks, s);
+        d1 = cr.dist(g, a1 ? sm.sel[j1] : cid, a1, nchunks, s);
+      }
       const bool p = (a0 && d0 * alpha < cd) || (a1 && d1 * alpha < cd);
       if (__any_sync(kFull, p)) { pruned = true; break; }
     }
     if (!pruned) {
       if (lane == 0) { sm.sel[ns] = cid; sm.sel_d[ns] = cd; }
+      if constexpr (kSel) {
+        if (lane < 4) cr.store_sel(sm.selrows, int(ns), nchunks, stride, swz, s);
+      }
       ns++;
       __syncwarp();
     }
@@ -192,7 +356,7 @@ __global__ void __launch_bounds__(128) batch_prune_kernel(GraphView g, uint32_t 
                                                           float alpha) {
   extern __shared__ __align__(16) char smem_raw[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  PruneSmem sm = prune_carve(smem_raw + prune_warp_bytes(g.dpad) * wid);
+  PruneSmem sm = prune_carve(smem_raw + prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) * wid, g.dpad);
   const uint32_t R = g.R;
   const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
   for (uint32_t b = blockIdx.x * (blockDim.x >> 5) + wid; b < bs; b += nwarps) {
@@ -259,7 +423,7 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
   extern __shared__ __align__(16) char smem_raw[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int tile = lane >> 2, s = lane & 3;
-  PruneSmem sm = prune_carve(smem_raw + prune_warp_bytes(g.dpad) * wid);
+  PruneSmem sm = prune_carve(smem_raw + prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) * wid, g.dpad);
   const uint32_t R = g.R;
   const uint32_t cap = 256 + R;  // MAX_CANDS of construct.cuh:574
   const uint32_t ng = *n_groups;
@@ -280,6 +444,9 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
           make_pair_key(bf16_bits_to_float(g.edist[size_t(l) * R + e]), id);
       nc += __popc(bal);
     }
+#ifdef JB_BUILD_CLOCKS
+    long long _c0 = clock64();
+#endif
     RowReg<MAXC, METRIC> tr;
     tr.load(g, t, nchunks, lane, sm.row);
     // The group is the contiguous run of keys with this target.
@@ -315,8 +482,23 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
       __syncwarp();
     }
     __syncwarp();
+#ifdef JB_BUILD_CLOCKS
+    long long _c1 = clock64();
+#endif
     sort_cands(sm.cand, nc, lane);
+#ifdef JB_BUILD_CLOCKS
+    long long _c2 = clock64();
+#endif
     prune_and_write<MAXC, METRIC>(g, t, sm, nc, alpha, lane);
+#ifdef JB_BUILD_CLOCKS
+    long long _c3 = clock64();
+    if (lane == 0) {
+      atomicAdd(&g_build_clk[0], (unsigned long long)(_c1 - _c0));
+      atomicAdd(&g_build_clk[1], (unsigned long long)(_c2 - _c1));
+      atomicAdd(&g_build_clk[2], (unsigned long long)(_c3 - _c2));
+      atomicAdd(&g_build_clk[3], 1ull);
+    }
+#endif
   }
 }
 
@@ -324,7 +506,7 @@ template <int MAXC, int METRIC>
 struct Kernels {
   static void prune(const GraphView& g, uint32_t off, uint32_t bs, const BuildWorkspace& ws,
                     float alpha, cudaStream_t st) {
-    const size_t smem = prune_warp_bytes(g.dpad) * 4;
+    const size_t smem = prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) * 4;
     auto k = batch_prune_kernel<MAXC, METRIC>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     const uint32_t blocks = (bs + 3) / 4;
@@ -333,7 +515,7 @@ struct Kernels {
   }
   static void reverse(const GraphView& g, size_t total, const BuildWorkspace& ws, float alpha,
                       cudaStream_t st) {
-    const size_t smem = prune_warp_bytes(g.dpad) * 4;
+    const size_t smem = prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) * 4;
     auto k = reverse_prune_kernel<MAXC, METRIC>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     int dev = 0, sms = 0, per_sm = 0;
@@ -368,6 +550,12 @@ void dispatch_prune(const GraphView& g, uint32_t off, uint32_t bs, const BuildWo
 }
 
 }  // namespace
+
+#ifdef JB_BUILD_CLOCKS
+extern "C" int jb_debug_build_clocks(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, g_build_clk, sizeof(unsigned long long) * 4) == cudaSuccess ? 0 : 1;
+}
+#endif
 
 uint32_t reference_max_batch_size(uint64_t budget_bytes, uint32_t n, uint32_t R) {
   // graph_construct_workspace::max_batch_size_for_budget (construct.cuh:233-258)

@@ -95,6 +95,15 @@ __device__ __forceinline__ float tile4_sum(float x) {
   return x;
 }
 
+// Same reduction when the tiles of a warp may be on different paths: only
+// the 4 lanes of the calling tile synchronise.
+__device__ __forceinline__ float tile4_sum_local(float x, int lane) {
+  const uint32_t mask = 0xFu << (lane & ~3);
+  x = __fadd_rn(x, __shfl_xor_sync(mask, x, 2));
+  x = __fadd_rn(x, __shfl_xor_sync(mask, x, 1));
+  return x;
+}
+
 // Warp-wide bitonic sort of 64 keys held two per lane (element p = r*32+lane).
 __device__ __forceinline__ void warp_sort64(uint64_t& v0, uint64_t& v1, int lane) {
 #pragma unroll

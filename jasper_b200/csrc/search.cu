@@ -183,7 +183,11 @@ __device__ __forceinline__ float2 h2f(uint32_t w) {
 template <int NQ, int METRIC>
 __device__ __forceinline__ float row_dist_lane(const float2* qp, const uint4* row, int nchunks) {
   float2 acc01 = make_float2(0.f, 0.f), acc23 = make_float2(0.f, 0.f);
-  constexpr int G = NQ < 4 ? NQ : 4;  // chunk quads per load group (4 * G loads in flight)
+#ifndef JB_LPR_GROUP
+#define JB_LPR_GROUP 4
+#endif
+  // chunk quads per load group (4 * G 16-byte loads in flight per lane)
+  constexpr int G = NQ < JB_LPR_GROUP ? NQ : JB_LPR_GROUP;
   if (METRIC == kL2) {
 #pragma unroll
     for (int g0 = 0; g0 < NQ; g0 += G) {
@@ -564,7 +568,10 @@ void launch_search(const SearchArgs& a, cudaStream_t stream) {
   if (a.bw + 64 >= 2048)
     throw std::invalid_argument("beam_width " + std::to_string(a.bw) +
                                 " is too large (beam_width + 64 must be < 2048)");
-  if (a.bw <= 64) return dispatch_dim<64, 11>(a, stream);
+#ifndef JB_HBITS64
+#define JB_HBITS64 11
+#endif
+  if (a.bw <= 64) return dispatch_dim<64, JB_HBITS64>(a, stream);
   if (a.bw <= 128) return dispatch_dim<128, 11>(a, stream);
   if (a.bw <= 256) return dispatch_dim<256, 11>(a, stream);
   if (a.bw <= 512) return dispatch_dim<512, 12>(a, stream);
