@@ -567,3 +567,283 @@ void orc_bruteforce(const uint16_t *base, uint32_t n, const uint16_t *queries,
   bf_ctx c = {base, n, queries, dpad, metric, k, out_idx, out_dist};
   parallel_for((long)nq, bf_body, &c);
 }
+
+/* ============================================================ directional */
+
+/* Round a double (holding an exact fp16 sum/difference/product) to fp16
+ * bits, round-to-nearest-even -- what __hsub2 / __hmul2 produce. */
+static uint16_t double_to_half_bits(double x) {
+  uint16_t sign = 0;
+  if (x < 0 || (x == 0 && signbit(x))) { sign = 0x8000; x = -x; }
+  if (x == 0) return sign;
+  if (x >= 65520.0) return sign | 0x7C00;               /* overflow -> inf */
+  int e;
+  double m = frexp(x, &e);                               /* x = m * 2^e, m in [0.5,1) */
+  int exp16 = e - 1 + 15;                                /* biased exponent of 1.xxx */
+  double scaled;
+  if (exp16 >= 1) scaled = ldexp(x, 10 - (e - 1));       /* mantissa incl. hidden bit */
+  else scaled = ldexp(x, 24);                            /* subnormal: units of 2^-24 */
+  double fl = floor(scaled);
+  double rem = scaled - fl;
+  uint64_t q = (uint64_t)fl;
+  if (rem > 0.5 || (rem == 0.5 && (q & 1))) q++;
+  (void)m;
+  if (exp16 >= 1) {
+    if (q == 2048) { q = 1024; exp16++; }
+    if (exp16 >= 31) return sign | 0x7C00;
+    return sign | (uint16_t)(exp16 << 10) | (uint16_t)(q & 0x3FF);
+  }
+  return sign | (uint16_t)q;                             /* q may reach 1024 = min normal */
+}
+
+/* Contraction variants of the reference's float expressions (which fused
+ * multiply-adds nvcc forms); the golden fixtures decide.  Bit 0-1: visit term
+ * `local += f0*f0 + f1*f1` (0: fma(f0,f0,f1*f1), 1: fma(f1,f1,f0*f0),
+ * 2: unfused); bit 2: LSH rank term fused; bit 3: L2 estimate fused. */
+static int g_dir_mode = 0 | 4 | 8;
+void orc_set_dir_mode(int m) { g_dir_mode = m; }
+
+/* Reduction of 128 per-thread partials as the reference's 128-thread blocks
+ * do it: xor butterfly (16, 8, 4, 2, 1) per warp, then the same butterfly
+ * over the 4 warp sums padded with zeros (beam_search_common.cuh:133-153). */
+static float block128_reduce(const float *part) {
+  float ws[32] = {0};
+  for (int w = 0; w < 4; w++) {
+    float v[32];
+    for (int l = 0; l < 32; l++) v[l] = part[w * 32 + l];
+    for (int d = 16; d > 0; d >>= 1) {
+      float nv[32];
+      for (int l = 0; l < 32; l++) nv[l] = v[l] + v[l ^ d];
+      memcpy(v, nv, sizeof(v));
+    }
+    ws[w] = v[0];
+  }
+  for (int d = 16; d > 0; d >>= 1) {
+    float nv[32];
+    for (int l = 0; l < 32; l++) nv[l] = ws[l] + ws[l ^ d];
+    memcpy(ws, nv, sizeof(ws));
+  }
+  return ws[0];
+}
+
+static float warp_reduce32(float *v) {
+  for (int d = 16; d > 0; d >>= 1) {
+    float nv[32];
+    for (int l = 0; l < 32; l++) nv[l] = v[l] + v[l ^ d];
+    memcpy(v, nv, 32 * sizeof(float));
+  }
+  return v[0];
+}
+
+typedef struct {
+  int kind;                 /* 0 = LSH, 1 = PQ */
+  uint32_t k_ranks;         /* LSH */
+  uint32_t packed_bytes;    /* 1 or 2 */
+  const void *packed;       /* [n][R * k_ranks] */
+  const uint16_t *mag_sq;   /* [n][R] bf16 */
+  const float *c;           /* [k_ranks] */
+  float norm_denom;
+  uint32_t pq_m, pq_dsub;   /* PQ */
+  const float *centroids;   /* [M][256][dsub] */
+  const uint8_t *codes;     /* [n][M * R] subspace-major */
+  const float *norms;       /* [n] */
+} orc_dir;
+
+/* compute_qu_diff_and_exact (beam_search_common.cuh:87-154); fills qu (fp16
+ * bits of q - u) for L2. */
+static float dir_visit_exact(const orc_graph *g, const uint16_t *q, uint32_t u, int ip,
+                             uint16_t *qu) {
+  float part[128];
+  memset(part, 0, sizeof(part));
+  const uint16_t *ur = row(g, u);
+  const uint32_t nv4 = g->dpad / 8;
+  for (uint32_t i = 0; i < nv4; i++) {
+    float local = part[i % 128];
+    for (int j = 0; j < 4; j++) {
+      double a0 = orc_half_to_float(q[8 * i + 2 * j]), a1 = orc_half_to_float(q[8 * i + 2 * j + 1]);
+      double b0 = orc_half_to_float(ur[8 * i + 2 * j]), b1 = orc_half_to_float(ur[8 * i + 2 * j + 1]);
+      if (!ip) {
+        uint16_t h0 = double_to_half_bits(a0 - b0), h1 = double_to_half_bits(a1 - b1);
+        if (qu) { qu[8 * i + 2 * j] = h0; qu[8 * i + 2 * j + 1] = h1; }
+        float f0 = orc_half_to_float(h0), f1 = orc_half_to_float(h1), t;
+        switch (g_dir_mode & 3) {
+          case 0: t = fmaf(f0, f0, f1 * f1); break;
+          case 1: t = fmaf(f1, f1, f0 * f0); break;
+          default: t = f0 * f0 + f1 * f1; break;
+        }
+        local = local + t;
+      } else {
+        float p0 = orc_half_to_float(double_to_half_bits(a0 * b0));
+        float p1 = orc_half_to_float(double_to_half_bits(a1 * b1));
+        local = local + (p0 + p1);
+      }
+    }
+    part[i % 128] = local;
+  }
+  return block128_reduce(part);
+}
+
+static void fr_insert(orc_entry *fr, uint32_t *fc, uint32_t k, uint32_t idx, float d) {
+  /* frontier_insert_sorted (beam_search_common.cuh:158-185): strict '>' */
+  uint32_t c = *fc;
+  int j;
+  if (c < k) {
+    j = (int)c;
+    while (j > 0 && fr[j - 1].dist > d) { fr[j] = fr[j - 1]; j--; }
+    fr[j].idx = idx; fr[j].dist = d;
+    *fc = c + 1;
+    return;
+  }
+  if (d >= fr[k - 1].dist) return;
+  j = (int)k - 1;
+  while (j > 0 && fr[j - 1].dist > d) { fr[j] = fr[j - 1]; j--; }
+  fr[j].idx = idx; fr[j].dist = d;
+}
+
+/* graph_beam_search_kernel (graph_beam_search.cuh:55-270) with the LSH
+ * (directional_beam_search.cuh:31-192) or PQ (pq_beam_search.cuh:31-201)
+ * estimator, for one query.  Unfilled outputs are (0x7FFFFFFF, FLT_MAX). */
+void orc_dir_search_one(const orc_graph *g, const orc_dir *dd, const uint16_t *q, uint32_t k,
+                        uint32_t bw, uint32_t limit, uint32_t max_result_size,
+                        uint32_t *out_idx, float *out_dist) {
+  const int ip = g->metric == 1;
+  const uint32_t R = g->R;
+  uint32_t cap = bw + 2 * R + 8;
+  orc_entry *buf = (orc_entry *)malloc(sizeof(orc_entry) * cap);
+  orc_entry *tmp = (orc_entry *)malloc(sizeof(orc_entry) * cap);
+  orc_entry *fr = (orc_entry *)malloc(sizeof(orc_entry) * (k + 1));
+  uint16_t *qu = (uint16_t *)calloc(g->dpad, sizeof(uint16_t));
+  float *lut = NULL;
+  float q_sq = 0.f, inv_nd = 0.f;
+  uint32_t fc = 0, count = 1;
+  buf[0].idx = g->medoid; buf[0].dist = 0.0f; buf[0].visited = 0;
+  if (dd->kind == 0) {
+    inv_nd = 1.0f / dd->norm_denom;
+  } else {
+    const uint32_t M = dd->pq_m, dsub = dd->pq_dsub;
+    lut = (float *)malloc(sizeof(float) * M * 256);
+    for (uint32_t e = 0; e < M * 256; e++) {       /* pq_build_lut: warp per centroid */
+      uint32_t j = e / 256;
+      float v[32];
+      for (int l = 0; l < 32; l++) {
+        float acc = 0.f;
+        for (uint32_t t = (uint32_t)l; t < dsub; t += 32)
+          acc = fmaf(orc_half_to_float(q[j * dsub + t]), dd->centroids[(size_t)e * dsub + t], acc);
+        v[l] = acc;
+      }
+      lut[e] = warp_reduce32(v);
+    }
+    if (!ip) {                                       /* ||q||^2, 128-thread block */
+      float part[128];
+      memset(part, 0, sizeof(part));
+      for (uint32_t i = 0; i < g->dpad; i++) {
+        float x = orc_half_to_float(q[i]);
+        part[i % 128] = fmaf(x, x, part[i % 128]);
+      }
+      q_sq = block128_reduce(part);
+    }
+  }
+  uint32_t visited_counter = 0, loop_count = 0;
+  const uint32_t lo = g->global_offset, hi = g->global_offset + g->n;
+  while (loop_count <= limit) {
+    loop_count++;
+    int f = -1;
+    for (uint32_t i = 0; i < count; i++) if (!buf[i].visited) { f = (int)i; break; }
+    if (f < 0) break;
+    buf[f].visited = 1;
+    const uint32_t u = buf[f].idx;
+    float exact_u, dist_u;
+    if (dd->kind == 0) {
+      exact_u = dir_visit_exact(g, q, u, ip, ip ? NULL : qu);
+      dist_u = ip ? -exact_u : exact_u;
+    } else {
+      exact_u = dir_visit_exact(g, q, u, 1, NULL);   /* <q, u> */
+      dist_u = ip ? -exact_u : (q_sq - 2.0f * exact_u) + dd->norms[u - g->global_offset];
+    }
+    fr_insert(fr, &fc, k, u, dist_u);
+    visited_counter++;
+    if (visited_counter == max_result_size) break;
+    const size_t lu = u - g->global_offset;
+    const uint32_t ne = g->counts[lu];
+    const uint32_t off = count;
+    for (uint32_t e = 0; e < ne; e++) {
+      uint32_t nb = g->edges[lu * R + e];
+      orc_entry en;
+      if (nb >= lo && nb < hi) { en.idx = nb; en.dist = 3.402823466e+38f; en.visited = 0; }
+      else { en.idx = ORC_EMPTY_IDX; en.dist = 3.402823466e+38f; en.visited = 1; }
+      buf[off + e] = en;
+    }
+    count += ne;
+    for (uint32_t e = 0; e < ne; e++) {
+      orc_entry *en = &buf[off + e];
+      if (en->idx == ORC_EMPTY_IDX) continue;
+      float est;
+      if (dd->kind == 0) {
+        float dot = 0.f;
+        for (uint32_t r = 0; r < dd->k_ranks; r++) {
+          uint32_t word, coord, neg;
+          if (dd->packed_bytes == 1) {
+            word = ((const uint8_t *)dd->packed)[lu * R * dd->k_ranks + e * dd->k_ranks + r];
+            coord = word & 0x7F; neg = word & 0x80;
+          } else {
+            word = ((const uint16_t *)dd->packed)[lu * R * dd->k_ranks + e * dd->k_ranks + r];
+            coord = word & 0x7FFF; neg = word & 0x8000;
+          }
+          float x = orc_half_to_float(ip ? q[coord] : qu[coord]);
+          float cs = dd->c[r] * (neg ? -1.0f : 1.0f);
+          dot = (g_dir_mode & 4) ? fmaf(cs, x, dot) : dot + cs * x;
+        }
+        float dot_est = dot * inv_nd;
+        float mag_sq = orc_bf16_to_float(dd->mag_sq[lu * R + e]);
+        float mag = sqrtf(mag_sq);
+        if (!ip) {
+          float base = exact_u + mag_sq;
+          est = (g_dir_mode & 8) ? fmaf(-(2.0f * mag), dot_est, base) : base - (2.0f * mag) * dot_est;
+        } else {
+          float ipv = fmaf(mag, dot_est, exact_u);
+          est = -ipv;
+        }
+      } else {
+        float acc = exact_u;
+        for (uint32_t j = 0; j < dd->pq_m; j++)
+          acc = acc + lut[j * 256 + dd->codes[lu * dd->pq_m * R + j * R + e]];
+        est = ip ? -acc : (q_sq - 2.0f * acc) + dd->norms[en->idx - g->global_offset];
+      }
+      en->dist = est;
+    }
+    stable_sort(buf, (int)count, tmp);
+    uint32_t w = 0;
+    for (uint32_t i = 0; i < count; i++) {
+      if (i > 0 && (buf[i].idx & 0x7FFFFFFFu) == (buf[i - 1].idx & 0x7FFFFFFFu)) continue;
+      buf[w++] = buf[i];
+    }
+    count = w;
+    if (count > bw) count = bw;
+  }
+  uint32_t out = 0;
+  for (uint32_t i = 0; i < fc && out < k; i++) {
+    uint32_t idx = fr[i].idx;
+    if (idx < lo || idx >= hi) continue;
+    if (is_deleted(g, idx)) continue;
+    out_idx[out] = idx; out_dist[out] = fr[i].dist; out++;
+  }
+  for (; out < k; out++) { out_idx[out] = ORC_EMPTY_IDX; out_dist[out] = 3.402823466e+38f; }
+  free(buf); free(tmp); free(fr); free(qu); free(lut);
+}
+
+typedef struct {
+  const orc_graph *g; const orc_dir *dd; const uint16_t *queries;
+  uint32_t k, bw, limit; uint32_t *oi; float *od;
+} dir_ctx;
+
+static void dir_body(void *vctx, long qi) {
+  dir_ctx *c = (dir_ctx *)vctx;
+  orc_dir_search_one(c->g, c->dd, c->queries + (size_t)qi * c->g->dpad, c->k, c->bw, c->limit,
+                     2048, c->oi + (size_t)qi * c->k, c->od + (size_t)qi * c->k);
+}
+
+void orc_dir_search(const orc_graph *g, const orc_dir *dd, const uint16_t *queries, uint32_t nq,
+                    uint32_t k, uint32_t bw, uint32_t limit, uint32_t *oi, float *od) {
+  dir_ctx c = {g, dd, queries, k, bw, limit, oi, od};
+  parallel_for((long)nq, dir_body, &c);
+}

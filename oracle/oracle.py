@@ -174,3 +174,53 @@ def reference_max_batch_size(budget_bytes: int, n: int, R: int) -> int:
     per_item = 8 * L + 8 * mrs + 4 + 8 * (mrs + R) + 4 + 8 * R + 4 * R + 4 * R
     b = 0 if budget_bytes <= 4 else (budget_bytes - 4) // per_item
     return min(b, n // 50)
+
+
+# ── directional search ──────────────────────────────────────────────────
+class _Dir(C.Structure):
+    _fields_ = [
+        ("kind", C.c_int), ("k_ranks", C.c_uint32), ("packed_bytes", C.c_uint32),
+        ("packed", C.c_void_p), ("mag_sq", C.c_void_p), ("c", C.c_void_p),
+        ("norm_denom", C.c_float), ("pq_m", C.c_uint32), ("pq_dsub", C.c_uint32),
+        ("centroids", C.c_void_p), ("codes", C.c_void_p), ("norms", C.c_void_p),
+    ]
+
+
+def set_dir_mode(m: int) -> None:
+    L = lib()
+    L.orc_set_dir_mode.argtypes = [C.c_int]
+    L.orc_set_dir_mode(int(m))
+
+
+def dir_search(g: OracleGraph, kind: str, art: dict, queries: np.ndarray, k: int,
+               beam_width: int, limit: int):
+    """directional_search ('lsh') or pq_search ('pq') given the artifacts."""
+    L = lib()
+    L.orc_dir_search.argtypes = [C.POINTER(_Graph), C.POINTER(_Dir), C.c_void_p, C.c_uint32,
+                                 C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
+    L.orc_dir_search.restype = None
+    keep = {}
+    def arr(name, dtype):
+        a = np.ascontiguousarray(art[name], dtype=dtype)
+        keep[name] = a
+        return _p(a)
+    d = _Dir()
+    if kind == "lsh":
+        packed = np.ascontiguousarray(art["lsh_packed"])
+        keep["packed"] = packed
+        d.kind, d.k_ranks, d.packed_bytes = 0, int(art["k_ranks"]), packed.dtype.itemsize
+        d.packed, d.mag_sq, d.c = _p(packed), arr("lsh_mag_sq", np.uint16), arr("lsh_c", np.float32)
+        d.norm_denom = float(art["lsh_norm_denom"])
+    else:
+        cent = np.ascontiguousarray(art["pq_centroids"], np.float32)
+        keep["cent"] = cent
+        M = int(art["k_ranks"])
+        d.kind, d.pq_m, d.pq_dsub = 1, M, cent.size // (M * 256)
+        d.centroids, d.codes, d.norms = _p(cent), arr("pq_codes", np.uint8), arr("norms", np.float32)
+    q = pad_rows(queries)
+    nq = q.shape[0]
+    oi = np.zeros((nq, k), np.uint32)
+    od = np.zeros((nq, k), np.float32)
+    gs = g._struct()
+    L.orc_dir_search(C.byref(gs), C.byref(d), _p(q), nq, k, beam_width, limit, _p(oi), _p(od))
+    return oi.view(np.int32), od

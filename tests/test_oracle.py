@@ -162,3 +162,25 @@ def test_golden_build_oracle_matches_reference(path):
     g = O.OracleGraph(X, int(z["R"]), metric=metric)
     g.build(float(z["alpha"]), O.reference_max_batch_size(10 * 10**9, int(z["n"]), int(z["R"])))
     golden_graph_equal(g, z)
+
+
+# ── directional fixtures (reference search on restated artifacts) ───────
+DIR_GOLDEN = GOLDEN / "directional"
+
+
+def dir_cases():
+    return sorted(DIR_GOLDEN.glob("*.npz"))
+
+
+@pytest.mark.parametrize("path", dir_cases(), ids=lambda p: p.stem)
+def test_golden_directional_oracle_matches_reference(path):
+    z = np.load(path)
+    X, Q = regen(z)
+    g = oracle_from_golden(z, X)
+    for kind, key in (("lsh", "directional_search"), ("pq", "pq_search")):
+        for bw in z["bws"]:
+            bw = int(bw)
+            oi, od = O.dir_search(g, kind, z, Q, 10, bw, 2 * bw)
+            np.testing.assert_array_equal(oi, z[f"{key}_idx_bw{bw}"], err_msg=f"{kind} bw={bw}")
+            np.testing.assert_array_equal(od.view(np.uint32), z[f"{key}_dist_bw{bw}"].view(np.uint32),
+                                          err_msg=f"{kind} bw={bw}")
