@@ -160,6 +160,47 @@ int jb_graph_get_edges(int64_t handle, uint32_t* edges, uint16_t* edge_dists, ui
  * graph::apply_global_offset, include/jasper/index/graph.cuh:801-827). */
 int jb_graph_apply_global_offset(int64_t handle, uint32_t offset);
 
+/* ── directional (LSH / PQ) ──────────────────────────────────────────── */
+
+#define JB_DIR_LSH 0
+#define JB_DIR_PQ 1
+
+/* Attach cross-polytope LSH edge payloads (host arrays): packed [n][R *
+ * k_ranks] words of packed_bytes (1: 7-bit coord, 2: 15-bit coord; sign in
+ * the top bit), mag_sq [n][R] bf16 bit patterns, c [k_ranks] and norm_denom
+ * (reference: edge_lsh_list + lsh_globals, include/jasper/lsh/edge_lsh.cuh:
+ * 9-80, lsh_globals.cuh:12-15; state kept per handle like dir_meta,
+ * ffi/jasper_ffi_common.cuh:135-149). */
+int jb_graph_set_lsh(int64_t handle, uint32_t k_ranks, uint32_t packed_bytes, const void* packed,
+                     const uint16_t* mag_sq, const float* c, float norm_denom);
+
+/* Attach PQ payloads (host arrays): centroids [m][256][dsub] f32, codes [n][m
+ * * R] (edge e of subspace j at j * R + e), exact norms [n] f32 (reference:
+ * pq_codebooks / edge_pq_list / graph::d_vector_norms,
+ * include/jasper/pq/pq_codebooks.cuh, edge_pq.cuh:23-50). */
+int jb_graph_set_pq(int64_t handle, uint32_t m, uint32_t dsub, const float* centroids,
+                    const uint8_t* codes, const float* norms);
+
+/* Which payloads a graph carries: bit 0 LSH, bit 1 PQ (reference:
+ * jasper_get_directional_flags_<cfg>, ffi/jasper_ffi_common.cuh:760-775). */
+int jb_graph_get_directional_flags(int64_t handle, int32_t* out_flags);
+
+/* The d x d random orthogonal prerotation for `seed` as float32, column-major
+ * (host memory, no GPU needed) -- the reference's set_rotation_matrix
+ * (include/jasper/rotation/rotation.cuh:74-110). */
+int jb_rotation_matrix(uint32_t dim, uint64_t seed, float* out);
+
+/* Directional search: kind JB_DIR_LSH (reference: DirectionalSearch_##id ->
+ * directional_search, ffi/jasper_ffi_common.cuh:530-609, beam_search/
+ * api.cuh:118-138) or JB_DIR_PQ (PqSearch_##id -> pq_search, :611-688,
+ * api.cuh:185-205).  Queries are rotated first when the graph was built with
+ * prerotation.  Device pointers; unfilled slots are (0x7FFFFFFF, FLT_MAX) as
+ * in the reference.  Asynchronous on `stream`. */
+int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* queries,
+                                uint64_t n_queries, uint32_t row_stride, int32_t* out_idx,
+                                float* out_dist, uint32_t k, uint32_t beam_width, uint32_t limit,
+                                void* stream);
+
 /* Merge per-shard top-k lists (device pointers, [n_shards][n_queries][k])
  * into the global top-k by (distance, id), on `stream`.  Used after the shards
  * of a range-sharded index are gathered on one GPU; no reference counterpart

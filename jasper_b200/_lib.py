@@ -57,6 +57,11 @@ SIGNATURES: dict[str, list] = {
     "jb_graph_set_edges": [_I64, _P, _P, _P, _U32],
     "jb_graph_get_edges": [_I64, _P, _P, _P],
     "jb_graph_apply_global_offset": [_I64, _U32],
+    "jb_rotation_matrix": [_U32, _U64, _P],
+    "jb_graph_set_lsh": [_I64, _U32, _U32, _P, _P, _P, C.c_float],
+    "jb_graph_set_pq": [_I64, _U32, _U32, _P, _P, _P],
+    "jb_graph_get_directional_flags": [_I64, C.POINTER(_I32)],
+    "jb_graph_directional_search": [_I64, _I32, _P, _U64, _U32, _P, _P, _U32, _U32, _U32, _P],
     "jb_merge_topk": [_P, _P, _U32, _U64, _U32, _P, _P, _P],
 }
 

@@ -14,6 +14,8 @@
 #include <vector>
 #include "../../include/jasper_b200.h"
 #include "construct.cuh"
+#include "dirsearch.cuh"
+#include "rotate.cuh"
 #include "jb_graph.h"
 #include "merge.cuh"
 #include "search.cuh"
@@ -421,6 +423,141 @@ int jb_graph_apply_global_offset(int64_t handle, uint32_t offset) {
     cuda_check(cudaMemcpy(g->edges, e.data(), nr * 4, cudaMemcpyDefault), "edges");
     g->medoid += delta;
     g->global_offset = offset;
+  });
+}
+
+int jb_rotation_matrix(uint32_t dim, uint64_t seed, float* out) {
+  return guarded([&] {
+    if (dim == 0 || !out) throw std::invalid_argument("dim must be > 0 and out non-null");
+    std::vector<float> P = jb::rotation_matrix_f32(int(dim), seed);
+    std::memcpy(out, P.data(), P.size() * sizeof(float));
+  });
+}
+
+int jb_graph_set_lsh(int64_t handle, uint32_t k_ranks, uint32_t packed_bytes, const void* packed,
+                     const uint16_t* mag_sq, const float* c, float norm_denom) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (k_ranks == 0 || k_ranks > 16) throw std::invalid_argument("k_ranks must be in [1, 16]");
+    if (packed_bytes != 1 && packed_bytes != 2) throw std::invalid_argument("packed_bytes must be 1 or 2");
+    if (packed_bytes == 1 && g->dpad > 128)
+      throw std::invalid_argument("1-byte LSH words address at most 128 coordinates");
+    if (!packed || !mag_sq || !c) throw std::invalid_argument("null argument");
+    jb::DirArtifacts& d = g->dir;
+    if (d.lsh_packed) { cudaFree(d.lsh_packed); d.lsh_packed = nullptr; }
+    if (d.lsh_mag) { cudaFree(d.lsh_mag); d.lsh_mag = nullptr; }
+    const size_t nw = size_t(g->n) * g->R * k_ranks;
+    cuda_check(cudaMalloc(&d.lsh_packed, nw * packed_bytes + 16), "alloc lsh words");
+    cuda_check(cudaMalloc(&d.lsh_mag, size_t(g->n) * g->R * 2 + 16), "alloc lsh magnitudes");
+    cuda_check(cudaMemcpy(d.lsh_packed, packed, nw * packed_bytes, cudaMemcpyDefault), "lsh words");
+    cuda_check(cudaMemcpy(d.lsh_mag, mag_sq, size_t(g->n) * g->R * 2, cudaMemcpyDefault), "lsh mags");
+    d.k_ranks = k_ranks;
+    d.packed_bytes = packed_bytes;
+    for (uint32_t r = 0; r < 16; r++) d.lsh_c[r] = r < k_ranks ? c[r] : 0.f;
+    d.norm_denom = norm_denom;
+    d.has_lsh = true;
+  });
+}
+
+int jb_graph_set_pq(int64_t handle, uint32_t m, uint32_t dsub, const float* centroids,
+                    const uint8_t* codes, const float* norms) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (m == 0 || dsub == 0 || m * dsub != g->dpad)
+      throw std::invalid_argument("PQ needs m * dsub == padded dim");
+    if (!centroids || !codes || !norms) throw std::invalid_argument("null argument");
+    jb::DirArtifacts& d = g->dir;
+    if (d.pq_centroids) { cudaFree(d.pq_centroids); d.pq_centroids = nullptr; }
+    if (d.pq_codes) { cudaFree(d.pq_codes); d.pq_codes = nullptr; }
+    if (d.norms) { cudaFree(d.norms); d.norms = nullptr; }
+    const size_t nc = size_t(m) * 256 * dsub, ncode = size_t(g->n) * g->R * m;
+    cuda_check(cudaMalloc(&d.pq_centroids, nc * 4), "alloc centroids");
+    cuda_check(cudaMalloc(&d.pq_codes, ncode + 16), "alloc codes");
+    cuda_check(cudaMalloc(&d.norms, size_t(g->n) * 4 + 16), "alloc norms");
+    cuda_check(cudaMemcpy(d.pq_centroids, centroids, nc * 4, cudaMemcpyDefault), "centroids");
+    cuda_check(cudaMemcpy(d.pq_codes, codes, ncode, cudaMemcpyDefault), "codes");
+    cuda_check(cudaMemcpy(d.norms, norms, size_t(g->n) * 4, cudaMemcpyDefault), "norms");
+    d.pq_m = m;
+    d.pq_dsub = dsub;
+    d.has_pq = true;
+  });
+}
+
+int jb_graph_get_directional_flags(int64_t handle, int32_t* out_flags) {
+  return guarded([&] {
+    if (!out_flags) throw std::invalid_argument("out_flags is null");
+    auto g = lookup(handle);
+    *out_flags = (g->dir.has_lsh ? 1 : 0) | (g->dir.has_pq ? 2 : 0);
+  });
+}
+
+int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* queries,
+                                uint64_t n_queries, uint32_t row_stride, int32_t* out_idx,
+                                float* out_dist, uint32_t k, uint32_t beam_width, uint32_t limit,
+                                void* stream) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (kind != JB_DIR_LSH && kind != JB_DIR_PQ) throw std::invalid_argument("kind must be LSH or PQ");
+    const jb::DirArtifacts& d = g->dir;
+    if (kind == JB_DIR_LSH && !d.has_lsh)
+      throw std::runtime_error("Graph " + std::to_string(handle) + " has no LSH artifacts built");
+    if (kind == JB_DIR_PQ && !d.has_pq)
+      throw std::runtime_error("Graph " + std::to_string(handle) + " has no PQ artifacts built");
+    if (n_queries == 0) return;
+    if (!queries || !out_idx || !out_dist) throw std::invalid_argument("null pointer argument");
+    if (row_stride < g->dim) throw std::invalid_argument("row_stride < dim");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    void* packed = nullptr;
+    void* counter = nullptr;
+    const uint16_t* q = queries;
+    const size_t qbytes = size_t(n_queries) * g->dpad * 2;
+    const bool aligned = (reinterpret_cast<uintptr_t>(queries) % 16) == 0;
+    if (row_stride != g->dpad || !aligned || d.prerotate) {
+      cuda_check(cudaMallocAsync(&packed, qbytes, st), "alloc queries");
+      cuda_check(cudaMemsetAsync(packed, 0, qbytes, st), "clear queries");
+      cuda_check(cudaMemcpy2DAsync(packed, size_t(g->dpad) * 2, queries, size_t(row_stride) * 2,
+                                   size_t(g->dim) * 2, n_queries, cudaMemcpyDefault, st),
+                 "pack queries");
+      if (d.prerotate) jb::rotate_rows_inplace(*g, static_cast<uint16_t*>(packed), n_queries, st);
+      q = static_cast<const uint16_t*>(packed);
+    }
+    cuda_check(cudaMallocAsync(&counter, 256, st), "alloc counter");
+    cuda_check(cudaMemsetAsync(counter, 0, 256, st), "clear counter");
+    jb::DirSearchArgs a{};
+    a.g = g->view();
+    a.kind = kind;
+    a.k_ranks = d.k_ranks;
+    a.packed_bytes = d.packed_bytes;
+    a.packed = d.lsh_packed;
+    a.mag = d.lsh_mag;
+    for (int r = 0; r < 16; r++) a.c[r] = d.lsh_c[r];
+    a.inv_norm_denom = d.has_lsh ? 1.0f / d.norm_denom : 0.f;
+    a.pq_m = d.pq_m;
+    a.pq_dsub = d.pq_dsub;
+    a.centroids = d.pq_centroids;
+    a.codes = d.pq_codes;
+    a.norms = d.norms;
+    a.queries = q;
+    a.nq = uint32_t(n_queries);
+    a.k = k;
+    a.bw = beam_width;
+    a.limit = limit;
+    a.max_result_size = 2048;
+    a.out_idx = out_idx;
+    a.out_dist = out_dist;
+    a.work_counter = static_cast<uint32_t*>(counter);
+    try {
+      jb::launch_dir_search(a, st);
+    } catch (...) {
+      cudaFreeAsync(counter, st);
+      if (packed) cudaFreeAsync(packed, st);
+      throw;
+    }
+    cudaFreeAsync(counter, st);
+    if (packed) cudaFreeAsync(packed, st);
   });
 }
 

@@ -86,7 +86,19 @@ void graph_allocate(Graph& g, uint32_t dim, uint32_t R, int metric, uint32_t n, 
   }
 }
 
+void graph_free_directional(Graph& g) {
+  DirArtifacts& d = g.dir;
+  if (d.lsh_packed) cudaFree(d.lsh_packed);
+  if (d.lsh_mag) cudaFree(d.lsh_mag);
+  if (d.pq_centroids) cudaFree(d.pq_centroids);
+  if (d.pq_codes) cudaFree(d.pq_codes);
+  if (d.norms) cudaFree(d.norms);
+  if (d.rotation) cudaFree(d.rotation);
+  d = DirArtifacts{};
+}
+
 void graph_free(Graph& g) {
+  graph_free_directional(g);
   free_array(g.vec, g.on_host);
   free_array(g.edges, g.on_host);
   free_array(g.edist, g.on_host);

@@ -40,6 +40,27 @@ struct GraphView {
   int ids_identity;
 };
 
+// Directional artifacts (reference: edge_lsh_list / edge_pq_list / lsh_globals
+// / pq_codebooks / graph::d_vector_norms, include/jasper/lsh/edge_lsh.cuh,
+// include/jasper/pq/edge_pq.cuh, include/jasper/index/graph.cuh:520-525).
+struct DirArtifacts {
+  bool has_lsh = false;
+  uint32_t k_ranks = 0;       // LSH ranks per edge (4 or 16)
+  uint32_t packed_bytes = 0;  // 1 (dim <= 128) or 2
+  void* lsh_packed = nullptr; // [n][R * k_ranks] words: sign in the MSB, coord below
+  uint16_t* lsh_mag = nullptr;// [n][R] bf16 |v - u|^2
+  float lsh_c[16] = {};
+  float norm_denom = 0.f;
+  bool has_pq = false;
+  uint32_t pq_m = 0, pq_dsub = 0;
+  float* pq_centroids = nullptr;  // [M][256][dsub]
+  uint8_t* pq_codes = nullptr;    // [n][M * R], code of edge e in subspace j at j * R + e
+  float* norms = nullptr;         // [n] exact |x|^2
+  bool prerotate = false;
+  uint64_t rotation_seed = 0;
+  uint16_t* rotation = nullptr;   // [dim][dim] fp16, column-major P (rows rotate as x^T P)
+};
+
 struct Graph {
   uint32_t dim = 0, dpad = 0, R = 0;
   int metric = kL2;
@@ -57,6 +78,7 @@ struct Graph {
   uint8_t* counts = nullptr;
   uint32_t* slot_to_id = nullptr;
   uint32_t* deleted = nullptr;
+  DirArtifacts dir;
 
   GraphView view() const {
     return GraphView{vec, edges, edist, counts, slot_to_id, deleted, n, dim, dpad, R,
@@ -75,5 +97,6 @@ void graph_upload_rows(Graph& g, const uint16_t* rows, uint32_t stride);
 void graph_load_file(Graph& g, const std::string& path, uint32_t dim, uint32_t R, int metric,
                      bool on_host);
 void graph_save_file(const Graph& g, const std::string& path);
+void graph_free_directional(Graph& g);
 
 }  // namespace jb

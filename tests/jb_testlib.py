@@ -67,3 +67,32 @@ def assert_same_results(ai, ad, bi, bd, msg=""):
     np.testing.assert_array_equal(ai, bi, err_msg=msg)
     np.testing.assert_array_equal(np.asarray(ad, np.float32).view(np.uint32),
                                   np.asarray(bd, np.float32).view(np.uint32), err_msg=msg)
+
+
+def set_artifacts(h: int, art: dict, k_ranks: int) -> None:
+    """Attach LSH and PQ payloads (numpy arrays, oracle/directional.py layout)."""
+    packed = np.ascontiguousarray(art["lsh_packed"])
+    mag = np.ascontiguousarray(art["lsh_mag_sq"], np.uint16)
+    c = np.ascontiguousarray(art["lsh_c"], np.float32)
+    _lib.call("jb_graph_set_lsh", h, k_ranks, packed.dtype.itemsize, packed.ctypes.data,
+              mag.ctypes.data, c.ctypes.data, float(art["lsh_norm_denom"]))
+    cent = np.ascontiguousarray(art["pq_centroids"], np.float32)
+    codes = np.ascontiguousarray(art["pq_codes"], np.uint8)
+    nrm = np.ascontiguousarray(art["norms"], np.float32)
+    M = k_ranks
+    _lib.call("jb_graph_set_pq", h, M, cent.size // (M * 256), cent.ctypes.data, codes.ctypes.data,
+              nrm.ctypes.data)
+
+
+def dir_search(h: int, kind: str, Q: np.ndarray, k: int, bw: int, limit: int | None = None):
+    import torch
+    q = torch.from_numpy(O.pad_rows(Q)).cuda()
+    nq = q.shape[0]
+    oi = torch.empty(nq, k, dtype=torch.int32, device="cuda")
+    od = torch.empty(nq, k, dtype=torch.float32, device="cuda")
+    limit = 2 * bw if limit is None else limit
+    _lib.call("jb_graph_directional_search", h, 0 if kind == "lsh" else 1, q.data_ptr(), nq,
+              q.shape[1], oi.data_ptr(), od.data_ptr(), k, bw, limit,
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return oi.cpu().numpy(), od.cpu().numpy()
