@@ -201,6 +201,57 @@ int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* qu
                                 float* out_dist, uint32_t k, uint32_t beam_width, uint32_t limit,
                                 void* stream);
 
+/* Build a graph for directional search (reference: ConstructDirectionalGraph_
+ * ##id, ffi/jasper_ffi_common.cuh:382-424).  With `prerotate` every row is
+ * first rotated by the prerotation of `prerotate_seed` (construct.cuh:
+ * 1019-1111) and the graph keeps the matrix to rotate queries; the caller's
+ * `vectors` are left unchanged (the reference rotates them in place).
+ * Synchronous. */
+int jb_graph_construct_directional(const uint16_t* vectors, uint64_t n, uint32_t dim,
+                                   uint32_t row_stride, uint32_t n_neighbors, int32_t metric,
+                                   double alpha, uint64_t workspace_budget_bytes, int32_t on_host,
+                                   int32_t prerotate, uint64_t prerotate_seed, void* stream,
+                                   int64_t* out_handle);
+
+/* Build the LSH payloads: k_ranks-rank cross-polytope sketch of every edge
+ * and the per-rank calibration from `n_samples` random edges (reference:
+ * BuildLsh_##id, ffi/jasper_ffi_common.cuh:426-444 -> generate_lsh_globals +
+ * populate_edge_lsh, graph.cuh:1153-1198, 1322-1370).  Synchronous. */
+int jb_graph_build_lsh(int64_t handle, uint32_t k_ranks, uint64_t n_samples, uint64_t seed);
+
+/* Build the PQ payloads: m x 256 codebooks by k-means on `n_train` sampled
+ * edge residuals, every edge's m-byte code and exact row norms (reference:
+ * BuildPq_##id, ffi/jasper_ffi_common.cuh:446-467 -> generate_pq_codebooks,
+ * populate_edge_pq, compute_vector_norms, graph.cuh:1142-1320).
+ * Synchronous. */
+int jb_graph_build_pq(int64_t handle, uint32_t m, uint64_t n_train, uint32_t kmeans_iter,
+                      uint64_t seed);
+
+/* Save the base graph plus the directional trailer (reference:
+ * SaveDirectionalGraph_##id -> save_directional_graph_to_file, graph.cuh:
+ * 1834-1937).  Synchronous. */
+int jb_graph_save_directional(int64_t handle, const char* path);
+
+/* Load a graph and its directional trailer, if any (reference:
+ * LoadDirectionalGraph_##id -> load_directional_graph_from_file, graph.cuh:
+ * 1939-2090).  `k_ranks` must match the file's LSH rank count / PQ
+ * subquantizer count; `prerotate` / `prerotate_seed` must match the build,
+ * as in the reference (they are not stored in the file).  Synchronous. */
+int jb_graph_load_directional(const char* path, uint32_t dim, uint32_t n_neighbors,
+                              int32_t metric, uint32_t k_ranks, int32_t on_host,
+                              int32_t prerotate, uint64_t prerotate_seed, int64_t* out_handle);
+
+/* Read the LSH payloads back into host arrays (shapes of jb_graph_set_lsh;
+ * c gets k_ranks floats).  The reference's counterpart is its debug dump
+ * (graph::dump_edge_lsh, graph.cuh:1372-1423).  Synchronous. */
+int jb_graph_get_lsh(int64_t handle, uint32_t* out_k_ranks, uint32_t* out_packed_bytes,
+                     void* packed, uint16_t* mag_sq, float* c, float* norm_denom);
+
+/* Read the PQ payloads back into host arrays (shapes of jb_graph_set_pq).
+ * Any output pointer may be NULL to skip it.  Synchronous. */
+int jb_graph_get_pq(int64_t handle, uint32_t* out_m, uint32_t* out_dsub, float* centroids,
+                    uint8_t* codes, float* norms);
+
 /* Merge per-shard top-k lists (device pointers, [n_shards][n_queries][k])
  * into the global top-k by (distance, id), on `stream`.  Used after the shards
  * of a range-sharded index are gathered on one GPU; no reference counterpart

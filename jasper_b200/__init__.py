@@ -124,21 +124,34 @@ class Graph:
              distance: DistanceFunc | str = DistanceFunc.L2, on_host: bool = False,
              k_ranks: int | None = None, prerotate: bool = False,
              prerotate_seed: int = 42) -> "Graph":
-        """Load a graph file (the reference's on-disk layout)."""
+        """Load a graph file (the reference's on-disk layout).  With ``k_ranks``
+        the file is read as a directional graph: its LSH / PQ trailer, if any,
+        is attached, and ``prerotate`` / ``prerotate_seed`` must repeat the
+        build's (they are not stored in the file, as in the reference)."""
         data_type = DataType(data_type)
         distance = DistanceFunc(distance)
-        if k_ranks is not None:
-            raise NotImplementedError("directional graphs are not available in this build")
-        config_id = _resolve_config(data_type, n_neighbors, distance)
         h = C.c_int64(-1)
-        _lib.call("jb_graph_load", str(path).encode(), dim, n_neighbors, _METRIC[distance],
-                  int(on_host), C.byref(h))
-        return cls(h.value, config_id, data_type, distance, n_neighbors, dim)
+        if k_ranks is None:
+            config_id = _resolve_config(data_type, n_neighbors, distance)
+            _lib.call("jb_graph_load", str(path).encode(), dim, n_neighbors, _METRIC[distance],
+                      int(on_host), C.byref(h))
+            return cls(h.value, config_id, data_type, distance, n_neighbors, dim)
+        config_id = _resolve_directional_config(data_type, n_neighbors, distance, k_ranks, dim)
+        _lib.call("jb_graph_load_directional", str(path).encode(), dim, n_neighbors,
+                  _METRIC[distance], int(k_ranks), int(on_host), int(bool(prerotate)),
+                  int(prerotate_seed), C.byref(h))
+        flags = C.c_int32(0)
+        _lib.call("jb_graph_get_directional_flags", h.value, C.byref(flags))
+        return cls(h.value, config_id, data_type, distance, n_neighbors, dim,
+                   is_directional=True, k_ranks=k_ranks, has_lsh=bool(flags.value & 1),
+                   has_pq=bool(flags.value & 2), prerotate=prerotate,
+                   prerotate_seed=prerotate_seed)
 
     def save(self, path: str) -> None:
         """Write this graph in the reference's on-disk layout."""
         self._check_alive()
-        _lib.call("jb_graph_save", self._handle, str(path).encode())
+        fn = "jb_graph_save_directional" if self._is_directional else "jb_graph_save"
+        _lib.call(fn, self._handle, str(path).encode())
 
     @classmethod
     def build(cls, vectors: torch.Tensor, n_neighbors: int = 32,
@@ -154,18 +167,32 @@ class Graph:
             raise ValueError(f"vectors must be 2D, got {vectors.ndim}D")
         if vectors.dtype != torch.float16:
             raise ValueError(f"Unsupported tensor dtype: {vectors.dtype}. Use torch.float16.")
-        if build_lsh or build_pq:
-            raise NotImplementedError("directional graphs are not available in this build")
         vectors = vectors.contiguous()
         n, dim = vectors.shape
-        config_id = _resolve_config(DataType.FLOAT16, n_neighbors, distance)
         h = C.c_int64(-1)
         stream = _stream_ptr(vectors.device) if vectors.is_cuda else 0
         if vectors.is_cuda:
             torch.cuda.set_device(vectors.device)
-        _lib.call("jb_graph_construct", _ptr(vectors), n, dim, dim, n_neighbors,
-                  _METRIC[distance], float(alpha), budget, int(on_host), stream, C.byref(h))
-        return cls(h.value, config_id, DataType.FLOAT16, distance, n_neighbors, dim)
+        if not (build_lsh or build_pq):
+            config_id = _resolve_config(DataType.FLOAT16, n_neighbors, distance)
+            _lib.call("jb_graph_construct", _ptr(vectors), n, dim, dim, n_neighbors,
+                      _METRIC[distance], float(alpha), budget, int(on_host), stream, C.byref(h))
+            return cls(h.value, config_id, DataType.FLOAT16, distance, n_neighbors, dim)
+        config_id = _resolve_directional_config(DataType.FLOAT16, n_neighbors, distance, k_ranks,
+                                                dim)
+        resolved_prerotate = True if prerotate is None else bool(prerotate)
+        _lib.call("jb_graph_construct_directional", _ptr(vectors), n, dim, dim, n_neighbors,
+                  _METRIC[distance], float(alpha), budget, int(on_host),
+                  int(resolved_prerotate), int(prerotate_seed), stream, C.byref(h))
+        g = cls(h.value, config_id, DataType.FLOAT16, distance, n_neighbors, dim,
+                is_directional=True, k_ranks=k_ranks, has_lsh=build_lsh, has_pq=build_pq,
+                prerotate=resolved_prerotate, prerotate_seed=prerotate_seed)
+        if build_lsh:
+            _lib.call("jb_graph_build_lsh", h.value, int(k_ranks), int(lsh_samples), int(lsh_seed))
+        if build_pq:
+            _lib.call("jb_graph_build_pq", h.value, int(k_ranks), int(pq_train),
+                      int(pq_kmeans_iter), int(pq_seed))
+        return g
 
     # ── properties ─────────────────────────────────────────────────────
     def _info(self) -> GraphInfo:
@@ -265,15 +292,48 @@ class Graph:
                   None if seen is None else _ptr(seen), _stream_ptr(queries.device))
         return out_i, out_d, stats
 
+    def _dir_search(self, kind: int, name: str, queries: torch.Tensor, k: int, beam_width: int,
+                    limit: int | None, print_throughput: bool):
+        queries = self._check_queries(queries)
+        nq = queries.size(0)
+        out_i = torch.empty(nq, k, dtype=torch.int32, device=queries.device)
+        out_d = torch.empty(nq, k, dtype=torch.float32, device=queries.device)
+        limit = beam_width * 2 if limit is None else limit
+        if print_throughput:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+        _lib.call("jb_graph_directional_search", self._handle, kind, _ptr(queries), nq,
+                  self._dim, _ptr(out_i), _ptr(out_d), k, beam_width, limit,
+                  _stream_ptr(queries.device))
+        if print_throughput:
+            e1.record()
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            print(f"[{name}] duration={ms}ms, throughput={nq * 1000.0 / max(ms, 1e-9)}")
+        return out_i, out_d
+
     def directional_search(self, queries: torch.Tensor, k: int = 10, beam_width: int = 64,
                            limit: int | None = None, print_throughput: bool = False):
-        raise RuntimeError("directional_search() requires a graph built with build_lsh=True "
-                           "(or loaded with LSH artifacts present)")
+        """Beam search scored by the cross-polytope LSH estimator (reference:
+        python/jasper/__init__.py:525-567).  Queries are rotated in the call
+        when the graph was prerotated.  ``limit`` defaults to 2 x beam_width."""
+        self._check_alive()
+        if not self._is_directional or not self._has_lsh:
+            raise RuntimeError("directional_search() requires a graph built with build_lsh=True "
+                               "(or loaded with LSH artifacts present)")
+        return self._dir_search(0, "directional_search", queries, k, beam_width, limit,
+                                print_throughput)
 
     def pq_search(self, queries: torch.Tensor, k: int = 10, beam_width: int = 64,
                   limit: int | None = None, print_throughput: bool = False):
-        raise RuntimeError("pq_search() requires a graph built with build_pq=True "
-                           "(or loaded with PQ artifacts present)")
+        """Beam search scored by the PQ ADC estimator (reference:
+        python/jasper/__init__.py:569-611)."""
+        self._check_alive()
+        if not self._is_directional or not self._has_pq:
+            raise RuntimeError("pq_search() requires a graph built with build_pq=True "
+                               "(or loaded with PQ artifacts present)")
+        return self._dir_search(1, "pq_search", queries, k, beam_width, limit, print_throughput)
 
     # ── rows, ids, deletion ───────────────────────────────────────────
     def get_vector(self, stable_id: int) -> torch.Tensor:

@@ -13,6 +13,7 @@
 #include <unordered_map>
 #include <vector>
 #include "../../include/jasper_b200.h"
+#include "builders.cuh"
 #include "construct.cuh"
 #include "dirsearch.cuh"
 #include "rotate.cuh"
@@ -568,6 +569,123 @@ int jb_merge_topk(const int32_t* shard_idx, const float* shard_dist, uint32_t n_
     if (!shard_idx || !shard_dist || !out_idx || !out_dist) throw std::invalid_argument("null argument");
     jb::launch_merge_topk(shard_idx, shard_dist, n_shards, n_queries, k, out_idx, out_dist,
                           static_cast<cudaStream_t>(stream));
+  });
+}
+
+int jb_graph_construct_directional(const uint16_t* vectors, uint64_t n, uint32_t dim,
+                                   uint32_t row_stride, uint32_t n_neighbors, int32_t metric,
+                                   double alpha, uint64_t workspace_budget_bytes, int32_t on_host,
+                                   int32_t prerotate, uint64_t prerotate_seed, void* stream,
+                                   int64_t* out_handle) {
+  return guarded([&] {
+    check_metric(metric);
+    if (out_handle == nullptr) throw std::invalid_argument("out_handle is null");
+    if (n > 0 && vectors == nullptr) throw std::invalid_argument("vectors is null");
+    if (row_stride < dim) throw std::invalid_argument("row_stride < dim");
+    if (n >= 0x7FFFFFFFull) throw std::invalid_argument("too many vectors");
+    auto g = std::make_shared<jb::Graph>();
+    jb::graph_allocate(*g, dim, n_neighbors, metric, uint32_t(n), on_host != 0);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    try {
+      jb::graph_upload_rows(*g, vectors, row_stride);
+      if (prerotate) {
+        jb::set_rotation(*g, prerotate_seed);
+        jb::rotate_rows_inplace(*g, g->vec, n, st);
+        cuda_check(cudaStreamSynchronize(st), "prerotate");
+      }
+      uint32_t mb = jb::reference_max_batch_size(workspace_budget_bytes, uint32_t(n), n_neighbors);
+      jb::construct_graph(*g, float(alpha), mb, st);
+    } catch (...) {
+      jb::graph_free(*g);
+      throw;
+    }
+    *out_handle = insert(g);
+  });
+}
+
+int jb_graph_build_lsh(int64_t handle, uint32_t k_ranks, uint64_t n_samples, uint64_t seed) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (n_samples == 0 || n_samples > 0xFFFFFFFFull)
+      throw std::invalid_argument("n_samples must be in [1, 2^32)");
+    cuda_check(cudaDeviceSynchronize(), "sync before build_lsh");
+    jb::build_lsh(*g, k_ranks, uint32_t(n_samples), seed, nullptr);
+  });
+}
+
+int jb_graph_build_pq(int64_t handle, uint32_t m, uint64_t n_train, uint32_t kmeans_iter,
+                      uint64_t seed) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (n_train > 0xFFFFFFFFull) throw std::invalid_argument("n_train must be below 2^32");
+    cuda_check(cudaDeviceSynchronize(), "sync before build_pq");
+    jb::build_pq(*g, m, uint32_t(n_train), kmeans_iter, seed, nullptr);
+  });
+}
+
+int jb_graph_save_directional(int64_t handle, const char* path) {
+  return guarded([&] {
+    if (path == nullptr) throw std::invalid_argument("path is null");
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    cuda_check(cudaDeviceSynchronize(), "sync before save");
+    jb::graph_save_directional(*g, path);
+  });
+}
+
+int jb_graph_load_directional(const char* path, uint32_t dim, uint32_t n_neighbors,
+                              int32_t metric, uint32_t k_ranks, int32_t on_host,
+                              int32_t prerotate, uint64_t prerotate_seed, int64_t* out_handle) {
+  return guarded([&] {
+    check_metric(metric);
+    if (path == nullptr || out_handle == nullptr) throw std::invalid_argument("null argument");
+    if (k_ranks == 0 || k_ranks > 16) throw std::invalid_argument("k_ranks must be in [1, 16]");
+    auto g = std::make_shared<jb::Graph>();
+    jb::graph_load_file(*g, path, dim, n_neighbors, metric, on_host != 0);
+    try {
+      jb::graph_load_directional(*g, path, k_ranks);
+      if (prerotate) jb::set_rotation(*g, prerotate_seed);
+    } catch (...) {
+      jb::graph_free(*g);
+      throw;
+    }
+    *out_handle = insert(g);
+  });
+}
+
+int jb_graph_get_lsh(int64_t handle, uint32_t* out_k_ranks, uint32_t* out_packed_bytes,
+                     void* packed, uint16_t* mag_sq, float* c, float* norm_denom) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    const jb::DirArtifacts& d = g->dir;
+    if (!d.has_lsh) throw std::runtime_error("Graph " + std::to_string(handle) + " has no LSH artifacts built");
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    if (out_k_ranks) *out_k_ranks = d.k_ranks;
+    if (out_packed_bytes) *out_packed_bytes = d.packed_bytes;
+    const size_t ne = size_t(g->n) * g->R;
+    if (packed) cuda_check(cudaMemcpy(packed, d.lsh_packed, ne * d.k_ranks * d.packed_bytes, cudaMemcpyDefault), "lsh words");
+    if (mag_sq) cuda_check(cudaMemcpy(mag_sq, d.lsh_mag, ne * 2, cudaMemcpyDefault), "lsh mags");
+    if (c) std::memcpy(c, d.lsh_c, 4 * d.k_ranks);
+    if (norm_denom) *norm_denom = d.norm_denom;
+  });
+}
+
+int jb_graph_get_pq(int64_t handle, uint32_t* out_m, uint32_t* out_dsub, float* centroids,
+                    uint8_t* codes, float* norms) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    const jb::DirArtifacts& d = g->dir;
+    if (!d.has_pq) throw std::runtime_error("Graph " + std::to_string(handle) + " has no PQ artifacts built");
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    if (out_m) *out_m = d.pq_m;
+    if (out_dsub) *out_dsub = d.pq_dsub;
+    if (centroids) cuda_check(cudaMemcpy(centroids, d.pq_centroids, size_t(d.pq_m) * 256 * d.pq_dsub * 4, cudaMemcpyDefault), "centroids");
+    if (codes) cuda_check(cudaMemcpy(codes, d.pq_codes, size_t(g->n) * g->R * d.pq_m, cudaMemcpyDefault), "codes");
+    if (norms && d.norms) cuda_check(cudaMemcpy(norms, d.norms, size_t(g->n) * 4, cudaMemcpyDefault), "norms");
   });
 }
 

@@ -256,4 +256,181 @@ void graph_save_file(const Graph& g, const std::string& path) {
   if (!f.good()) throw std::runtime_error("write failed for " + path);
 }
 
+// ---------------------------------------------------------------------------
+// Directional trailer (include/jasper/index/graph.cuh:1814-2090):
+//   u32 magic 0x484C5344 | u32 version 1 | u8 flags (1 lsh, 2 pq, 4 norms)
+//   lsh:  u8 k_ranks | u8 packed word size | f32 c[k_ranks] | f32 norm_denom |
+//         n records { word[R * k_ranks] | bf16 mag[R] } padded to 4 bytes
+//   pq:   u32 M | u32 K (256) | u32 dsub | f32 centroids[M][K][dsub] |
+//         n records { u8 code[M * R] } padded to 4 bytes
+//   norms: f32[n]
+// The trailer follows the complete base section (records, deletion bitmask,
+// next_id).  The reference's loader looks for it at 32 + n * (legacy record
+// size) instead, which only lands on it for legacy-layout base sections;
+// graph_load_directional accepts the trailer at either offset.
+
+namespace {
+
+constexpr uint32_t kTrailerMagic = 0x484C5344u;
+constexpr uint32_t kTrailerVersion = 1u;
+
+size_t pad4(size_t x) { return (x + 3) / 4 * 4; }
+
+}  // namespace
+
+void graph_save_directional(const Graph& g, const std::string& path) {
+  graph_save_file(g, path);
+  const DirArtifacts& d = g.dir;
+  if (g.n == 0) return;
+  const bool has_lsh = d.has_lsh, has_pq = d.has_pq, has_norms = d.norms != nullptr;
+  if (!has_lsh && !has_pq && !has_norms) return;
+  std::ofstream f(path, std::ios::binary | std::ios::app);
+  if (!f.is_open()) throw std::runtime_error("cannot reopen " + path + " for the trailer");
+  const uint8_t flags = uint8_t((has_lsh ? 1 : 0) | (has_pq ? 2 : 0) | (has_norms ? 4 : 0));
+  f.write(reinterpret_cast<const char*>(&kTrailerMagic), 4);
+  f.write(reinterpret_cast<const char*>(&kTrailerVersion), 4);
+  f.write(reinterpret_cast<const char*>(&flags), 1);
+  const size_t n = g.n, R = g.R;
+  if (has_lsh) {
+    const uint8_t kr = uint8_t(d.k_ranks), ps = uint8_t(d.packed_bytes);
+    f.write(reinterpret_cast<const char*>(&kr), 1);
+    f.write(reinterpret_cast<const char*>(&ps), 1);
+    f.write(reinterpret_cast<const char*>(d.lsh_c), 4 * d.k_ranks);
+    f.write(reinterpret_cast<const char*>(&d.norm_denom), 4);
+    const size_t wbytes = R * d.k_ranks * d.packed_bytes, rec = pad4(wbytes + 2 * R);
+    std::vector<char> words(n * wbytes), mags(n * R * 2), out(n * rec, 0);
+    copy_to(words.data(), d.lsh_packed, words.size());
+    copy_to(mags.data(), d.lsh_mag, mags.size());
+    for (size_t i = 0; i < n; i++) {
+      memcpy(&out[i * rec], &words[i * wbytes], wbytes);
+      memcpy(&out[i * rec + wbytes], &mags[i * R * 2], R * 2);
+    }
+    f.write(out.data(), std::streamsize(out.size()));
+  }
+  if (has_pq) {
+    const uint32_t hdr[3] = {d.pq_m, 256u, d.pq_dsub};
+    f.write(reinterpret_cast<const char*>(hdr), sizeof(hdr));
+    std::vector<float> cent(size_t(d.pq_m) * 256 * d.pq_dsub);
+    copy_to(cent.data(), d.pq_centroids, cent.size() * 4);
+    f.write(reinterpret_cast<const char*>(cent.data()), std::streamsize(cent.size() * 4));
+    const size_t cbytes = R * d.pq_m, rec = pad4(cbytes);
+    std::vector<char> codes(n * cbytes), out(n * rec, 0);
+    copy_to(codes.data(), d.pq_codes, codes.size());
+    for (size_t i = 0; i < n; i++) memcpy(&out[i * rec], &codes[i * cbytes], cbytes);
+    f.write(out.data(), std::streamsize(out.size()));
+  }
+  if (has_norms) {
+    std::vector<float> nr(n);
+    copy_to(nr.data(), d.norms, n * 4);
+    f.write(reinterpret_cast<const char*>(nr.data()), std::streamsize(n * 4));
+  }
+  if (!f.good()) throw std::runtime_error("write failed for " + path);
+}
+
+namespace {
+
+template <typename T>
+void read_exact(std::ifstream& f, T* dst, size_t bytes, const std::string& path) {
+  f.read(reinterpret_cast<char*>(dst), std::streamsize(bytes));
+  if (size_t(f.gcount()) != bytes)
+    throw std::runtime_error("short read in the directional trailer of " + path);
+}
+
+template <typename T>
+T* device_copy(const void* src, size_t bytes, const char* what) {
+  void* p = nullptr;
+  check(cudaMalloc(&p, bytes + 16), what);
+  check(cudaMemcpy(p, src, bytes, cudaMemcpyHostToDevice), what);
+  return static_cast<T*>(p);
+}
+
+}  // namespace
+
+int graph_load_directional(Graph& g, const std::string& path, uint32_t k_ranks) {
+  std::ifstream f(path, std::ios::binary | std::ios::ate);
+  if (!f.is_open()) throw std::runtime_error("Failed to open " + path);
+  const uint64_t size = uint64_t(f.tellg());
+  f.seekg(0);
+  uint64_t hdr[4];
+  read_exact(f, hdr, sizeof(hdr), path);
+  const uint64_t n = hdr[1], bpn = hdr[3];
+  const uint64_t legacy = 2ull * g.dim + 1 + 6ull * g.R;
+  const bool has_id = bpn == legacy + 4 || bpn == legacy + 5;
+  uint64_t full_end = 32 + n * bpn;
+  if (bpn == legacy + 4) full_end += (n + 7) / 8;
+  if (has_id) full_end += 8;
+  const uint64_t offsets[2] = {full_end, 32 + n * legacy};
+  int64_t at = -1;
+  for (uint64_t off : offsets) {
+    if (off + 9 > size) continue;
+    f.seekg(std::streamoff(off));
+    uint32_t mv[2];
+    read_exact(f, mv, 8, path);
+    if (mv[0] == kTrailerMagic && mv[1] == kTrailerVersion) { at = int64_t(off); break; }
+  }
+  if (at < 0 || n == 0) return 0;
+  f.seekg(std::streamoff(at + 8));
+  uint8_t flags = 0;
+  read_exact(f, &flags, 1, path);
+  DirArtifacts& d = g.dir;
+  const size_t R = g.R;
+  if (flags & 1) {
+    uint8_t kr = 0, ps = 0;
+    read_exact(f, &kr, 1, path);
+    read_exact(f, &ps, 1, path);
+    const uint32_t want_ps = g.dpad <= 128 ? 1u : 2u;
+    if (kr != k_ranks || ps != want_ps)
+      throw std::runtime_error("directional trailer of " + path + ": k_ranks/packed word size " +
+                               std::to_string(kr) + "/" + std::to_string(ps) +
+                               " do not match the requested " + std::to_string(k_ranks) + "/" +
+                               std::to_string(want_ps));
+    float c[17] = {};
+    read_exact(f, c, 4 * (size_t(kr) + 1), path);
+    const size_t wbytes = R * kr * ps, rec = pad4(wbytes + 2 * R);
+    std::vector<char> in(n * rec), words(n * wbytes), mags(n * R * 2);
+    read_exact(f, in.data(), in.size(), path);
+    for (size_t i = 0; i < n; i++) {
+      memcpy(&words[i * wbytes], &in[i * rec], wbytes);
+      memcpy(&mags[i * R * 2], &in[i * rec + wbytes], R * 2);
+    }
+    if (d.lsh_packed) cudaFree(d.lsh_packed);
+    if (d.lsh_mag) cudaFree(d.lsh_mag);
+    d.lsh_packed = device_copy<void>(words.data(), words.size(), "upload lsh words");
+    d.lsh_mag = device_copy<uint16_t>(mags.data(), mags.size(), "upload lsh magnitudes");
+    for (uint32_t r = 0; r < 16; r++) d.lsh_c[r] = r < kr ? c[r] : 0.f;
+    d.norm_denom = c[kr];
+    d.k_ranks = kr;
+    d.packed_bytes = ps;
+    d.has_lsh = true;
+  }
+  if (flags & 2) {
+    uint32_t ph[3];
+    read_exact(f, ph, sizeof(ph), path);
+    if (ph[0] != k_ranks || ph[1] != 256u || ph[0] == 0 || ph[0] * ph[2] != g.dpad)
+      throw std::runtime_error("directional trailer of " + path + ": PQ M/K/dsub " +
+                               std::to_string(ph[0]) + "/" + std::to_string(ph[1]) + "/" +
+                               std::to_string(ph[2]) + " do not match this graph");
+    std::vector<float> cent(size_t(ph[0]) * 256 * ph[2]);
+    read_exact(f, cent.data(), cent.size() * 4, path);
+    const size_t cbytes = R * ph[0], rec = pad4(cbytes);
+    std::vector<char> in(n * rec), codes(n * cbytes);
+    read_exact(f, in.data(), in.size(), path);
+    for (size_t i = 0; i < n; i++) memcpy(&codes[i * cbytes], &in[i * rec], cbytes);
+    if (d.pq_centroids) cudaFree(d.pq_centroids);
+    if (d.pq_codes) cudaFree(d.pq_codes);
+    d.pq_centroids = device_copy<float>(cent.data(), cent.size() * 4, "upload centroids");
+    d.pq_codes = device_copy<uint8_t>(codes.data(), codes.size(), "upload codes");
+    d.pq_m = ph[0];
+    d.pq_dsub = ph[2];
+    d.has_pq = true;
+  }
+  if (flags & 4) {
+    std::vector<float> nr(n);
+    read_exact(f, nr.data(), n * 4, path);
+    if (d.norms) cudaFree(d.norms);
+    d.norms = device_copy<float>(nr.data(), n * 4, "upload norms");
+  }
+  return flags;
+}
+
 }  // namespace jb

@@ -98,5 +98,10 @@ void graph_load_file(Graph& g, const std::string& path, uint32_t dim, uint32_t R
                      bool on_host);
 void graph_save_file(const Graph& g, const std::string& path);
 void graph_free_directional(Graph& g);
+// Base file plus the directional trailer (LSH / PQ / norms present in g.dir).
+void graph_save_directional(const Graph& g, const std::string& path);
+// Read the directional trailer of `path` into g.dir (g already loaded from the
+// same file).  Returns the trailer flags (0 when the file has none).
+int graph_load_directional(Graph& g, const std::string& path, uint32_t k_ranks);
 
 }  // namespace jb

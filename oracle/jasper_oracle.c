@@ -847,3 +847,96 @@ void orc_dir_search(const orc_graph *g, const orc_dir *dd, const uint16_t *queri
   dir_ctx c = {g, dd, queries, k, bw, limit, oi, od};
   parallel_for((long)nq, dir_body, &c);
 }
+
+/* ---- directional artifact builders (exact parts) ----------------------- */
+
+/* populate_lsh (include/jasper/lsh/lsh_kernels.cuh:9-131), 128 threads:
+ * Δ = v − u in fp16; key = |Δ| half bits << (B+1) | sign << B | coord with
+ * B = 7 (packed_bytes 1) or 15; Σ float(Δ)² with thread t (= i mod 128)
+ * accumulating fmaf(f, f, acc) and the two-level block butterfly; k_ranks
+ * rounds of argmax, the winner's low B+1 bits stored, then zeroed.  Only edge
+ * slots below the edge count are written. */
+typedef struct { const orc_graph *g; uint32_t k_ranks; int pb; void *packed; uint16_t *mag; } lsh_ctx;
+
+static void lsh_body(void *vctx, long l) {
+  lsh_ctx *c = (lsh_ctx *)vctx;
+  const orc_graph *g = c->g;
+  const uint32_t B = c->pb == 1 ? 7u : 15u, cmask = (1u << B) - 1u;
+  const uint16_t *u = g->vec + (size_t)l * g->dpad;
+  uint32_t *keys = (uint32_t *)malloc(sizeof(uint32_t) * g->dpad);
+  for (uint32_t e = 0; e < g->counts[l]; e++) {
+    const uint32_t nb = g->edges[(size_t)l * g->R + e];
+    const uint16_t *v = row(g, nb);
+    float part[128] = {0};
+    for (uint32_t i = 0; i < g->dpad; i++) {
+      uint16_t h = double_to_half_bits((double)orc_half_to_float(v[i]) - (double)orc_half_to_float(u[i]));
+      keys[i] = ((uint32_t)(h & 0x7FFFu) << (B + 1)) | ((uint32_t)((h >> 15) & 1u) << B) | (i & cmask);
+      float f = orc_half_to_float(h);
+      part[i % 128] = fmaf(f, f, part[i % 128]);
+    }
+    float m2 = block128_reduce(part);
+    for (uint32_t r = 0; r < c->k_ranks; r++) {
+      uint32_t best = 0;
+      for (uint32_t i = 0; i < g->dpad; i++) if (keys[i] > best) best = keys[i];
+      size_t w = ((size_t)l * g->R + e) * c->k_ranks + r;
+      if (c->pb == 1) ((uint8_t *)c->packed)[w] = (uint8_t)best;
+      else ((uint16_t *)c->packed)[w] = (uint16_t)best;
+      keys[best & cmask] = 0;
+    }
+    c->mag[(size_t)l * g->R + e] = orc_float_to_bf16(m2);
+  }
+  free(keys);
+}
+
+void orc_lsh_edges(const orc_graph *g, uint32_t k_ranks, int packed_bytes, void *packed,
+                   uint16_t *mag) {
+  lsh_ctx c = {g, k_ranks, packed_bytes, packed, mag};
+  parallel_for((long)g->n, lsh_body, &c);
+}
+
+/* pq_populate (include/jasper/pq/pq_kernels.cuh:252-295): residual
+ * float(fp16(v − u)); per subspace, d_c = Σ_t fmaf(r_t − C_t, ·, d) in t
+ * order; the lowest (d, c) wins (pq_block_argmin, :25-58). */
+typedef struct { const orc_graph *g; uint32_t M; const float *cent; uint8_t *codes; } pqc_ctx;
+
+static void pqc_body(void *vctx, long l) {
+  pqc_ctx *c = (pqc_ctx *)vctx;
+  const orc_graph *g = c->g;
+  const uint32_t dsub = g->dpad / c->M;
+  const uint16_t *u = g->vec + (size_t)l * g->dpad;
+  float *res = (float *)malloc(sizeof(float) * g->dpad);
+  for (uint32_t e = 0; e < g->counts[l]; e++) {
+    const uint16_t *v = row(g, g->edges[(size_t)l * g->R + e]);
+    for (uint32_t i = 0; i < g->dpad; i++)
+      res[i] = orc_half_to_float(double_to_half_bits((double)orc_half_to_float(v[i]) -
+                                                     (double)orc_half_to_float(u[i])));
+    for (uint32_t j = 0; j < c->M; j++) {
+      float best = 0; int bi = -1;
+      for (int cc = 0; cc < 256; cc++) {
+        const float *C = c->cent + ((size_t)j * 256 + cc) * dsub;
+        float d = 0.0f;
+        for (uint32_t t = 0; t < dsub; t++) { float df = res[j * dsub + t] - C[t]; d = fmaf(df, df, d); }
+        if (bi < 0 || d < best) { best = d; bi = cc; }
+      }
+      c->codes[(size_t)l * c->M * g->R + (size_t)j * g->R + e] = (uint8_t)bi;
+    }
+  }
+  free(res);
+}
+
+void orc_pq_codes(const orc_graph *g, uint32_t M, const float *cent, uint8_t *codes) {
+  pqc_ctx c = {g, M, cent, codes};
+  parallel_for((long)g->n, pqc_body, &c);
+}
+
+/* pq_compute_vector_norms (pq_kernels.cuh:218-247), 128 threads. */
+void orc_row_norms(const orc_graph *g, float *norms) {
+  for (uint32_t l = 0; l < g->n; l++) {
+    float part[128] = {0};
+    for (uint32_t i = 0; i < g->dpad; i++) {
+      float v = orc_half_to_float(g->vec[(size_t)l * g->dpad + i]);
+      part[i % 128] = fmaf(v, v, part[i % 128]);
+    }
+    norms[l] = block128_reduce(part);
+  }
+}

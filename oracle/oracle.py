@@ -224,3 +224,42 @@ def dir_search(g: OracleGraph, kind: str, art: dict, queries: np.ndarray, k: int
     gs = g._struct()
     L.orc_dir_search(C.byref(gs), C.byref(d), _p(q), nq, k, beam_width, limit, _p(oi), _p(od))
     return oi.view(np.int32), od
+
+
+# ── directional artifact builders (the exact, sampling-free parts) ───────
+def lsh_edges_exact(g: OracleGraph, k_ranks: int):
+    """populate_lsh per edge: words [n, R * k_ranks] (uint8 for dpad <= 128,
+    else uint16) and bf16 |Δ|² [n, R], bit-exact to the device builder."""
+    L = lib()
+    L.orc_lsh_edges.argtypes = [C.POINTER(_Graph), C.c_uint32, C.c_int, C.c_void_p, C.c_void_p]
+    L.orc_lsh_edges.restype = None
+    pb = 1 if g.dpad <= 128 else 2
+    packed = np.zeros((g.n, g.R * k_ranks), np.uint8 if pb == 1 else np.uint16)
+    mag = np.zeros((g.n, g.R), np.uint16)
+    gs = g._struct()
+    L.orc_lsh_edges(C.byref(gs), int(k_ranks), pb, _p(packed), _p(mag))
+    return packed, mag
+
+
+def pq_codes_exact(g: OracleGraph, centroids: np.ndarray):
+    """pq_populate: codes [n, M * R] (subspace-major) for given centroids."""
+    L = lib()
+    L.orc_pq_codes.argtypes = [C.POINTER(_Graph), C.c_uint32, C.c_void_p, C.c_void_p]
+    L.orc_pq_codes.restype = None
+    cent = np.ascontiguousarray(centroids, np.float32)
+    M = cent.shape[0]
+    codes = np.zeros((g.n, M * g.R), np.uint8)
+    gs = g._struct()
+    L.orc_pq_codes(C.byref(gs), M, _p(cent), _p(codes))
+    return codes
+
+
+def row_norms_exact(g: OracleGraph):
+    """pq_compute_vector_norms: exact |x|² per row, block-reduction order."""
+    L = lib()
+    L.orc_row_norms.argtypes = [C.POINTER(_Graph), C.c_void_p]
+    L.orc_row_norms.restype = None
+    out = np.zeros(g.n, np.float32)
+    gs = g._struct()
+    L.orc_row_norms(C.byref(gs), _p(out))
+    return out

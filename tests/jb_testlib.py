@@ -96,3 +96,57 @@ def dir_search(h: int, kind: str, Q: np.ndarray, k: int, bw: int, limit: int | N
               torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     return oi.cpu().numpy(), od.cpu().numpy()
+
+
+def get_artifacts(h: int, n: int, R: int, dpad: int) -> dict:
+    """Read back LSH and PQ payloads (whichever the graph carries)."""
+    flags = C.c_int32(0)
+    _lib.call("jb_graph_get_directional_flags", h, C.byref(flags))
+    art = {}
+    if flags.value & 1:
+        kr, pb, nd = C.c_uint32(0), C.c_uint32(0), C.c_float(0)
+        _lib.call("jb_graph_get_lsh", h, C.byref(kr), C.byref(pb), None, None, None, C.byref(nd))
+        packed = np.zeros((n, R * kr.value), np.uint8 if pb.value == 1 else np.uint16)
+        mag = np.zeros((n, R), np.uint16)
+        c = np.zeros(kr.value, np.float32)
+        _lib.call("jb_graph_get_lsh", h, None, None, packed.ctypes.data, mag.ctypes.data,
+                  c.ctypes.data, C.byref(nd))
+        art.update(lsh_packed=packed, lsh_mag_sq=mag, lsh_c=c, lsh_norm_denom=np.float32(nd.value),
+                   k_ranks=kr.value)
+    if flags.value & 2:
+        m, ds = C.c_uint32(0), C.c_uint32(0)
+        _lib.call("jb_graph_get_pq", h, C.byref(m), C.byref(ds), None, None, None)
+        cent = np.zeros((m.value, 256, ds.value), np.float32)
+        codes = np.zeros((n, m.value * R), np.uint8)
+        nrm = np.zeros(n, np.float32)
+        _lib.call("jb_graph_get_pq", h, None, None, cent.ctypes.data, codes.ctypes.data,
+                  nrm.ctypes.data)
+        art.update(pq_centroids=cent, pq_codes=codes, norms=nrm, k_ranks=m.value)
+    return art
+
+
+def get_rows(h: int, n: int, dim: int) -> np.ndarray:
+    """All stored rows (identity ids) as fp16 [n, dim]."""
+    out = np.zeros((n, dim), np.float16)
+    for i in range(n):
+        _lib.call("jb_graph_get_vector", h, i, out[i:].ctypes.data)
+    return out
+
+
+def construct_directional(X: np.ndarray, R: int, metric: int, alpha: float, prerotate: bool,
+                          seed: int = 42, budget: int = 10 * 10**9) -> int:
+    x = np.ascontiguousarray(X, dtype=np.float16)
+    h = C.c_int64(-1)
+    _lib.call("jb_graph_construct_directional", x.ctypes.data, x.shape[0], x.shape[1], x.shape[1],
+              R, metric, float(alpha), budget, 0, int(prerotate), seed, None, C.byref(h))
+    return h.value
+
+
+def oracle_from_handle(h: int, n: int, dim: int, R: int, metric: int) -> "O.OracleGraph":
+    """Copy a handle's rows and adjacency into an oracle graph."""
+    info = _lib.GraphInfo()
+    _lib.call("jb_graph_get_info", h, C.byref(info))
+    g = O.OracleGraph(get_rows(h, n, dim), R, metric=metric, medoid=info.medoid)
+    e, d, c = get_edges(h, n, R)
+    g.edges[:], g.edist[:], g.counts[:] = e, d, c
+    return g
