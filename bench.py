@@ -62,60 +62,69 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+    """SM clock and clock-event reasons sampled through NVML every ~2 ms on a
+    background thread while the timed region runs (NVML reads only; no
+    setting of the GPU is touched)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
+    def __init__(self, device: torch.device, period_s: float = 0.002):
+        self.device = device
+        self.period = period_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self.handle = None
+        self._stop = threading.Event()
+        self.t = None
+
+    def _open(self):
+        import pynvml
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.device)
+        try:
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        return pynvml
+
+    def _run(self, nv):
+        while True:
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                self.samples.append((mhz, rs))
+            except Exception:
+                pass
+            if self._stop.wait(self.period):
+                break
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            nv = self._open()
+            self.t = threading.Thread(target=self._run, args=(nv,), daemon=True)
             self.t.start()
-        except OSError:
-            self.proc = None
+        except Exception:
+            self.t = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self.t is not None:
+            self.t.join(timeout=1.0)
 
     def summary(self):
-        mhz, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            p = [x.strip() for x in ln.split(",")]
-            if len(p) < 9:
-                continue
-            try:
-                mhz.append(float(p[1]))
-                mx = max(mx, float(p[2]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, p[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        if not mhz:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": float(np.median(mhz)), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(mhz)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        mhz = [m for m, _ in self.samples]
+        active = 0
+        for _, r in self.samples:
+            active |= r
+        reasons = sorted(k for k, bit in self.REASONS.items() if active & bit)
+        return {"sm_mhz": float(np.median(mhz)), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(mhz), "sm_mhz_min": int(min(mhz)), "source": "nvml"}
 
 
 def flush_l2(buf: torch.Tensor):
@@ -228,7 +237,7 @@ def run_jasper(args):
         dist.barrier()
     torch.cuda.synchronize()
     times = {bw: [] for bw in pair}
-    with ClockSampler(dev.index if ws == 1 else local) as clk:
+    with ClockSampler(dev) as clk:
         t0 = time.perf_counter()
         for _ in range(args.steps):
             step(times)
@@ -252,19 +261,20 @@ def run_jasper(args):
     out_i = torch.empty(args.nq, K, dtype=torch.int32).pin_memory()
     out_d = torch.empty(args.nq, K, dtype=torch.float32).pin_memory()
     e2e_ms = {}
-    for bw in pair:
-        for _ in range(2):
-            _lib.call("jb_graph_search_host", g._handle, q_host.data_ptr(), args.nq, 128,
-                      out_i.data_ptr(), out_d.data_ptr(), K, bw, 2 * bw, stream.cuda_stream)
-        ts = []
-        for _ in range(args.steps):
-            flush_l2(flush)
-            torch.cuda.synchronize()
-            t1 = time.perf_counter()
-            _lib.call("jb_graph_search_host", g._handle, q_host.data_ptr(), args.nq, 128,
-                      out_i.data_ptr(), out_d.data_ptr(), K, bw, 2 * bw, stream.cuda_stream)
-            ts.append(time.perf_counter() - t1)
-        e2e_ms[bw] = 1e3 * float(np.mean(ts))
+    with ClockSampler(dev) as clk_e2e:
+        for bw in pair:
+            for _ in range(max(2, args.warmup)):
+                _lib.call("jb_graph_search_host", g._handle, q_host.data_ptr(), args.nq, 128,
+                          out_i.data_ptr(), out_d.data_ptr(), K, bw, 2 * bw, stream.cuda_stream)
+            ts = []
+            for _ in range(max(args.steps, 10)):
+                flush_l2(flush)
+                torch.cuda.synchronize()
+                t1 = time.perf_counter()
+                _lib.call("jb_graph_search_host", g._handle, q_host.data_ptr(), args.nq, 128,
+                          out_i.data_ptr(), out_d.data_ptr(), K, bw, 2 * bw, stream.cuda_stream)
+                ts.append(time.perf_counter() - t1)
+            e2e_ms[bw] = 1e3 * float(np.median(ts))
     if dist is not None:
         t = torch.tensor([e2e_ms[bw] for bw in pair], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -311,7 +321,9 @@ def run_jasper(args):
                                "time = max over ranks") if ws > 1 else "single GPU"},
             "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
                     "h2d_bytes_per_step": int(len(pair) * args.nq * 128 * 2),
-                    "d2h_bytes_per_step": int(len(pair) * args.nq * K * 8)},
+                    "d2h_bytes_per_step": int(len(pair) * args.nq * K * 8),
+                    "timing": "median host wall time of jb_graph_search_host per call",
+                    "clocks": clk_e2e.summary()},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "gpu_launches": args.steps * len(pair),
@@ -353,6 +365,184 @@ def cpu_baseline(g, base_np, q_np, lo, hi, recalls, args):
                       f"per run, beam widths {sorted({lo, hi})}, all host threads"}
 
 
+# ── config 5: range-sharded index (one shard per GPU) ─────────────────────
+def gen_sift_like_gpu(n: int, dim: int, n_centers: int, seed: int, dev) -> torch.Tensor:
+    """SIFT-like rows generated on the GPU (config 5 at 12.5M rows per shard):
+    a Gaussian mixture of n_centers centres with uniform integer coordinates
+    in [0, 128], uniform cluster choice, per-dimension sigma 12, rounded and
+    clipped to [0, 255].  Same distribution as jasper_b200.synthetic.sift_like
+    (which draws with numpy); the centres depend on the seed only."""
+    gc = torch.Generator(device=dev).manual_seed(1_000_003)
+    centers = torch.randint(0, 129, (n_centers, dim), generator=gc, device=dev).float()
+    g = torch.Generator(device=dev).manual_seed(seed)
+    out = torch.empty(n, dim, dtype=torch.float16, device=dev)
+    for i in range(0, n, 1 << 20):
+        m = min(1 << 20, n - i)
+        c = torch.randint(0, n_centers, (m,), generator=g, device=dev)
+        x = centers[c] + 12.0 * torch.randn(m, dim, generator=g, device=dev)
+        out[i:i + m] = x.round_().clamp_(0, 255).half()
+    return out
+
+
+def exact_topk_shard(base: torch.Tensor, queries: torch.Tensor, k: int, offset: int):
+    """Exact L2 top-k of every query over one shard (fp32; exact for integer
+    rows), ids global.  Blocks of 1000 queries x 1M rows bound the scratch."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    out_i, out_d = [], []
+    for q0 in range(0, queries.size(0), 1000):
+        qf = queries[q0:q0 + 1000].float()
+        qn = (qf * qf).sum(1, keepdim=True)
+        best_d = torch.full((qf.size(0), k), float("inf"), device=base.device)
+        best_i = torch.full((qf.size(0), k), -1, dtype=torch.int64, device=base.device)
+        for b0 in range(0, base.size(0), 1 << 20):
+            b = base[b0:b0 + (1 << 20)].float()
+            d = qn + (b * b).sum(1)[None, :] - 2.0 * (qf @ b.T)
+            dk, ik = d.topk(k, dim=1, largest=False)
+            cd = torch.cat([best_d, dk], 1)
+            ci = torch.cat([best_i, ik + b0 + offset], 1)
+            best_d, sel = cd.topk(k, dim=1, largest=False)
+            best_i = ci.gather(1, sel)
+        out_i.append(best_i.int())
+        out_d.append(best_d)
+    return torch.cat(out_i), torch.cat(out_d)
+
+
+def run_sharded(args):
+    """Config 5: every rank builds a range shard of args.n_shard rows (global
+    ids rank * n_shard + i) concurrently; each query batch goes to every
+    rank, per-shard top-k are gathered to rank 0 over NCCL and merged there
+    (jb_merge_topk).  Weak scaling: the index grows with the number of GPUs."""
+    from jasper_b200 import sharded
+    ws, rank, local = dist_env()
+    dist = None
+    if ws > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    n_shard = args.n_shard
+    n_total = n_shard * ws
+    offset = rank * n_shard
+    base = gen_sift_like_gpu(n_shard, 128, 65536, 8 + 1000 * rank, dev)
+    queries = gen_sift_like_gpu(args.nq, 128, 65536, 9, dev)   # identical on every rank
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(vals):
+        t = torch.tensor(vals, device=dev, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    sg = sharded.ShardedGraph.build(base, offset, n_total, n_neighbors=64, distance="l2",
+                                    alpha=1.2)
+    e1.record()
+    barrier()
+    (build_s,) = max_over_ranks([e0.elapsed_time(e1) / 1e3])
+
+    gi, gd = exact_topk_shard(base, queries, K, offset)
+    if ws > 1:
+        got = sharded.gather_topk(gi, gd, root=0)
+        gt = sharded.merge_topk(got[0], got[1])[0] if rank == 0 else None
+    else:
+        gt = gi
+
+    def search(bw):
+        if ws > 1:
+            return sg.search(queries, k=K, beam_width=bw, root=0)
+        return sg.search_local(queries, k=K, beam_width=bw)
+
+    recalls = {}
+    for bw in BWS:
+        res = search(bw)
+        r = recall_at_k(res[0], gt) if rank == 0 else 0.0
+        recalls[bw] = r
+    t = torch.tensor([recalls[bw] for bw in BWS], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.broadcast(t, 0)
+    recalls = {bw: v for bw, v in zip(BWS, t.tolist())}
+    lo, hi = bracket(recalls)
+    pair = (lo, hi) if lo != hi else (hi,)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        for bw in pair:
+            search(bw)
+    barrier()
+    times = {bw: [] for bw in pair}
+    with ClockSampler(dev) as clk:
+        for _ in range(args.steps):
+            for bw in pair:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                search(bw)
+                b.record(stream)
+                times[bw].append((a, b))
+        torch.cuda.synchronize()
+    barrier()
+    ms_local = [sum(x.elapsed_time(y) for x, y in times[bw]) / args.steps for bw in pair]
+    ms = dict(zip(pair, max_over_ranks(ms_local)))
+    qps = {bw: args.nq / (ms[bw] / 1e3) for bw in pair}
+    value = interp_qps(recalls[lo], qps[lo], recalls[hi], qps[hi])
+
+    # e2e: queries from pinned host memory, the merged top-k back to the host
+    q_host = queries.cpu().pin_memory()
+    e2e = {}
+    for bw in pair:
+        ts = []
+        for _ in range(max(args.steps, 5)):
+            barrier()
+            t1 = time.perf_counter()
+            qd = q_host.to(dev, non_blocking=True)
+            res = sg.search(qd, k=K, beam_width=bw, root=0) if ws > 1 else \
+                sg.search_local(qd, k=K, beam_width=bw)
+            if res is not None:
+                res[0].cpu(), res[1].cpu()
+            torch.cuda.synchronize()
+            ts.append(time.perf_counter() - t1)
+        e2e[bw] = float(np.median(ts)) * 1e3
+    e2e = dict(zip(pair, max_over_ranks([e2e[bw] for bw in pair])))
+    e2e_qps = {bw: args.nq / (e2e[bw] / 1e3) for bw in pair}
+    e2e_value = interp_qps(recalls[lo], e2e_qps[lo], recalls[hi], e2e_qps[hi])
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "queries/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sum(ms.values()), 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 rows, f32 distances", "data": "synthetic",
+            "config": {"workload": f"config5: range-sharded {n_total} x 128 SIFT-like fp16 "
+                                   f"({ws} shards x {n_shard}), L2, R=64, alpha=1.2, "
+                                   f"{args.nq} queries broadcast, k=10, NCCL gather + device merge",
+                       "n_base": n_total, "rows_per_gpu": n_shard, "queries": args.nq,
+                       "bracket_beam_widths": list(pair), "limit": "2*beam_width",
+                       "parallelism": f"range shards x{ws}",
+                       "l2": "inputs larger than L2 (3.2 GB of rows per GPU)"},
+            "recall_at_10": {str(b): round(r, 4) for b, r in recalls.items()},
+            "qps": {str(b): round(v, 1) for b, v in qps.items()},
+            "build": {"mvec_per_s": round(n_total / build_s / 1e6, 4),
+                      "seconds": round(build_s, 3),
+                      "note": f"{ws} shards built concurrently; time = max over ranks"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
+                    "h2d_bytes_per_step": int(len(pair) * args.nq * 128 * 2),
+                    "d2h_bytes_per_step": int(len(pair) * args.nq * K * 8)},
+            "gpu_launches": args.steps * len(pair) * (2 if ws > 1 else 1),
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    sg.free()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 # ── reference arm ─────────────────────────────────────────────────────────
 def run_reference(args):
     ws, rank, local = dist_env()
@@ -391,7 +581,7 @@ def run_reference(args):
             search(h, queries, oi, od, K, bw, 2 * bw, False)
     torch.cuda.synchronize()
     ts = {bw: [] for bw in pair}
-    with ClockSampler(0) as clk:
+    with ClockSampler(torch.device("cuda", 0)) as clk:
         for _ in range(args.steps):
             for bw in pair:
                 flush_l2(flush)
@@ -441,11 +631,17 @@ def main():
     ap.add_argument("--nq", type=int, default=10_000)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", default="replicas", choices=["replicas", "sharded"],
+                    help="replicas: config 2 per GPU (default); sharded: config 5 range shards")
+    ap.add_argument("--n-shard", type=int, default=12_500_000,
+                    help="rows per GPU in --mode sharded (config 5: 12.5M)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.mode == "sharded":
+        run_sharded(args)
     else:
         run_jasper(args)
 

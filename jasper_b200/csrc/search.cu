@@ -83,7 +83,7 @@ __host__ __device__ inline size_t warp_smem_bytes(uint32_t bwcap, uint32_t hbits
   b = align16(b);
   // lane-per-row query pairs: 2 * nq chunk pairs x 8 float2
   if (smem_query) b += align16(sizeof(uint16_t) * dpad);
-  else b += size_t(128) * nq;
+  else b += size_t(128) * nq + 64;  // query pairs, or the tile layout's padded chains
   return b;
 }
 
@@ -247,12 +247,88 @@ __device__ __forceinline__ float row_dist_lane(const float2* qp, const uint4* ro
   return METRIC == kL2 ? r : -r;
 }
 
+// ── tile-of-4 distances (L2, dpad <= 128) ──────────────────────────────────
+// The reference's own lane layout: lane s of a 4-lane tile accumulates
+// partial sum s of a row (16-byte chunks s, s+4, ..., one fma per element)
+// and the tile ends with (s0 + s2) + (s1 + s3).  Here each tile carries four
+// rows at once (rows t, t+8, t+16, t+24 of a 32-row round; 16 loads in
+// flight per lane for dpad = 128) and packs two rows into one f32x2 chain,
+// so a round of 32 rows costs the same math as lane-per-row but a short
+// round (few candidates left) only costs the slots it uses.
+// qtile layout: qt[s * QS + k * 8 + e] = -q[(s + 4k) * 8 + e], zeros past the
+// row, QS = 8 * NQ + 4 (the pad staggers the four chains across banks).
+#ifndef JB_T4_SLOTS
+#define JB_T4_SLOTS 2  // rows per tile per round: 16 rows per warp, 8 loads per lane at dpad 128
+#endif
+
+template <int NQ>
+__device__ __forceinline__ void build_qtile(float* qt, const uint16_t* qrow, int nchunks, int lane) {
+  const __half* qh = reinterpret_cast<const __half*>(qrow);
+  constexpr int QS = 8 * NQ + 4;
+  for (int t = lane; t < 4 * QS; t += 32) {
+    const int ch = t / QS, r = t % QS, k = r >> 3, e = r & 7;
+    const int c = ch + 4 * k;
+    qt[t] = (r < 8 * NQ && c < nchunks) ? -__half2float(qh[c * 8 + e]) : 0.f;
+  }
+}
+
+template <int NQ>
+__device__ __forceinline__ float2 tile4_pair_sum(float2 v) {
+  float2 w = make_float2(__shfl_xor_sync(kFull, v.x, 2), __shfl_xor_sync(kFull, v.y, 2));
+  v = __fadd2_rn(v, w);
+  w = make_float2(__shfl_xor_sync(kFull, v.x, 1), __shfl_xor_sync(kFull, v.y, 1));
+  return __fadd2_rn(v, w);
+}
+
+template <int NQ>
+__device__ __forceinline__ float2 tile4_pair_chain(const float* qs, const uint4 (&ua)[NQ],
+                                                   const uint4 (&ub)[NQ]) {
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < NQ; k++) {
+    const float4 q0 = *reinterpret_cast<const float4*>(qs + k * 8);
+    const float4 q1 = *reinterpret_cast<const float4*>(qs + k * 8 + 4);
+    const float qv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint32_t aw[4] = {ua[k].x, ua[k].y, ua[k].z, ua[k].w};
+    const uint32_t bw[4] = {ub[k].x, ub[k].y, ub[k].z, ub[k].w};
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+      const float2 fa = h2f(aw[w]), fb = h2f(bw[w]);
+      const float2 d0 = __fadd2_rn(make_float2(fa.x, fb.x), make_float2(qv[2 * w], qv[2 * w]));
+      acc = __ffma2_rn(d0, d0, acc);
+      const float2 d1 = __fadd2_rn(make_float2(fa.y, fb.y), make_float2(qv[2 * w + 1], qv[2 * w + 1]));
+      acc = __ffma2_rn(d1, d1, acc);
+    }
+  }
+  return acc;
+}
+
 #ifndef JB_SEARCH_MIN_BLOCKS
 #define JB_SEARCH_MIN_BLOCKS 4
 #endif
+#ifndef JB_COUNT_MERGE
+#define JB_COUNT_MERGE 32
+#endif
+// Up to this many kept candidates are merged by counting instead of sorting.
+constexpr int kCountMerge = JB_COUNT_MERGE;
+#ifndef JB_TILE_MIN_BLOCKS
+#define JB_TILE_MIN_BLOCKS 6
+#endif
+// The tile path fits in 80 registers; shared memory then allows 5 CTAs per SM.
+template <int MAXC, int METRIC>
+constexpr int search_min_blocks() {
+  return (MAXC > 0 && MAXC <= 4 && METRIC == kL2) ? JB_TILE_MIN_BLOCKS : JB_SEARCH_MIN_BLOCKS;
+}
+
 template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC>
-__global__ void __launch_bounds__(128, JB_SEARCH_MIN_BLOCKS) beam_search_warp_kernel(SearchArgs a) {
+__global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC>())
+    beam_search_warp_kernel(SearchArgs a) {
   constexpr bool kRegQ = (MAXC > 0);
+#ifndef JB_NO_TILE4
+  constexpr bool kTile = (MAXC > 0 && MAXC <= 4 && METRIC == kL2);
+#else
+  constexpr bool kTile = false;
+#endif
   extern __shared__ __align__(16) char smem_raw[];
   const int lane = threadIdx.x & 31;
   const int wid = threadIdx.x >> 5;
@@ -276,7 +352,10 @@ __global__ void __launch_bounds__(128, JB_SEARCH_MIN_BLOCKS) beam_search_warp_ke
     const uint16_t* qrow = a.use_range
         ? g.vec + size_t(a.query_start + q - g.global_offset) * dpad
         : a.queries + size_t(q) * dpad;
-    if constexpr (kRegQ) {
+    if constexpr (kTile) {
+      build_qtile<MAXC>(reinterpret_cast<float*>(sm.qpairs), qrow, nchunks, lane);
+      __syncwarp();
+    } else if constexpr (kRegQ) {
       build_qpairs<MAXC, METRIC>(sm.qpairs, qrow, nchunks, lane);
       __syncwarp();
     } else {
@@ -292,12 +371,54 @@ __global__ void __launch_bounds__(128, JB_SEARCH_MIN_BLOCKS) beam_search_warp_ke
     uint64_t* cur = sm.beam0;
     uint64_t* nxt = sm.beam1;
     uint32_t cnt = 0;
+    int pos = -1;  // beam position of the node being expanded
     // Evaluates sm.cand_ids[0, m), then keeps only candidates that can enter
     // the beam -- with the beam full, a key above its bw-th entry would land
     // past position bw in the merged order and be clipped -- and leaves them
     // sorted in sm.cand_keys.  Returns how many were kept.
     auto evaluate_and_sort = [&](int m) -> int {
-      if constexpr (kRegQ) {
+      if constexpr (kTile) {
+        const float* qs = reinterpret_cast<const float*>(sm.qpairs) + s * (8 * MAXC + 4);
+        constexpr int SL = JB_T4_SLOTS;  // rows per tile per round
+        for (int base = 0; base < m; base += 8 * SL) {
+          const int nslot = min(SL, (m - base + 7) >> 3);  // warp-uniform
+          uint4 u[SL][MAXC];
+          uint32_t rid[SL];
+#pragma unroll
+          for (int i = 0; i < SL; i++) {
+            const int j = base + tile + 8 * i;
+            const bool act = i < nslot && j < m;
+            rid[i] = act ? sm.cand_ids[j] : kInvalid;
+            const uint4* row = reinterpret_cast<const uint4*>(
+                g.vec + size_t(act ? rid[i] - g.global_offset : 0) * dpad);
+#pragma unroll
+            for (int k = 0; k < MAXC; k++) {
+              const int c = s + 4 * k;
+              u[i][k] = (act && c < nchunks) ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+            }
+          }
+#pragma unroll
+          for (int p = 0; p < SL / 2; p++) {
+            if (2 * p >= nslot) break;
+            const float2 v = tile4_pair_sum<MAXC>(tile4_pair_chain<MAXC>(qs, u[2 * p], u[2 * p + 1]));
+            if (s == 0) {
+#pragma unroll
+              for (int h = 0; h < 2; h++) {
+                const int i = 2 * p + h;
+                const int j = base + tile + 8 * i;
+                if (rid[i] != kInvalid) {
+                  sm.cand_keys[j] = make_key(h ? v.y : v.x, rid[i]);
+                  if (a.seen_bits != nullptr) {
+                    uint32_t* bits = a.seen_bits + size_t(q) * ((g.n + 31) / 32);
+                    const uint32_t l = rid[i] - g.global_offset;
+                    if (!(atomicOr(&bits[l >> 5], 1u << (l & 31)) & (1u << (l & 31)))) first_evals++;
+                  }
+                }
+              }
+            }
+          }
+        }
+      } else if constexpr (kRegQ) {
         // One lane per candidate row (32 rows per pass).
         for (int base = 0; base < m; base += 32) {
           const int j = base + lane;
@@ -352,6 +473,7 @@ __global__ void __launch_bounds__(128, JB_SEARCH_MIN_BLOCKS) beam_search_warp_ke
         if (v0 != kKeyMax) sm.cand_keys[__popc(k0 & lt)] = v0;
         if (v1 != kKeyMax) sm.cand_keys[__popc(k0) + __popc(k1 & lt)] = v1;
         __syncwarp();
+        if (kept <= kCountMerge) return kept;  // left unsorted: merged by counting
         uint64_t v = lane < kept ? sm.cand_keys[lane] : kKeyMax;
         v = warp_sort32(v, lane);
         sm.cand_keys[lane] = v;
@@ -383,7 +505,7 @@ __global__ void __launch_bounds__(128, JB_SEARCH_MIN_BLOCKS) beam_search_warp_ke
     while (loop_count <= a.limit) {
       loop_count++;
       // choose_new_frontier: first unvisited entry of the sorted beam.
-      int pos = -1;
+      pos = -1;
       for (uint32_t base = 0; base < cnt; base += 32) {
         const uint32_t i = base + lane;
         const bool unv = i < cnt && !key_visited(cur[i]);
@@ -419,12 +541,12 @@ __global__ void __launch_bounds__(128, JB_SEARCH_MIN_BLOCKS) beam_search_warp_ke
       // add_frontier_out: the neighbour list of u, in-range ids not seen before.
       const uint32_t lu = u - g.global_offset;
       const uint32_t ne = g.counts[lu];
-      deg_sum += ne;
       const uint32_t* el = g.edges + size_t(lu) * R;
       // Issued together with the count load (slots past the count are masked
       // below), so the two dependent gathers overlap.
       uint32_t nb0 = lane < R ? __ldg(el + lane) : kInvalid;
       uint32_t nb1 = lane + 32 < R ? __ldg(el + lane + 32) : kInvalid;
+      deg_sum += ne;
       bool f0 = (lane < ne) && (nb0 - g.global_offset < g.n) && hash_insert(sm.hash, HBITS, nb0);
       const uint32_t b0 = __ballot_sync(kFull, f0);
       bool f1 = (lane + 32 < ne) && (nb1 - g.global_offset < g.n) && hash_insert(sm.hash, HBITS, nb1);
@@ -442,15 +564,33 @@ __global__ void __launch_bounds__(128, JB_SEARCH_MIN_BLOCKS) beam_search_warp_ke
       if (kept == 0) continue;
 
       // Merge beam (cnt) and kept candidates by rank; keep the first bw.
-      for (uint32_t i = lane; i < cnt; i += 32) {
-        const uint64_t b = cur[i];
-        const uint32_t p = i + lower_rank(sm.cand_keys, kept, b);
-        if (p < bw) nxt[p] = b;
-      }
-      for (int j = lane; j < kept; j += 32) {
-        const uint64_t c = sm.cand_keys[j];
-        const uint32_t p = j + lower_rank(cur, int(cnt), c);
-        if (p < bw) nxt[p] = c;
+      // A few kept candidates stay unsorted: each position is counted
+      // directly (keys are distinct, so every rank is exact).
+      if (kept <= kCountMerge) {
+        for (uint32_t i = lane; i < cnt; i += 32) {
+          const uint64_t b = cur[i];
+          uint32_t r = 0;
+          for (int j = 0; j < kept; j++) r += sm.cand_keys[j] < b;
+          if (i + r < bw) nxt[i + r] = b;
+        }
+        if (lane < kept) {
+          const uint64_t c = sm.cand_keys[lane];
+          uint32_t r = 0;
+          for (int j = 0; j < kept; j++) r += sm.cand_keys[j] < c;
+          const uint32_t p = r + lower_rank(cur, int(cnt), c);
+          if (p < bw) nxt[p] = c;
+        }
+      } else {
+        for (uint32_t i = lane; i < cnt; i += 32) {
+          const uint64_t b = cur[i];
+          const uint32_t p = i + lower_rank(sm.cand_keys, kept, b);
+          if (p < bw) nxt[p] = b;
+        }
+        for (int j = lane; j < kept; j += 32) {
+          const uint64_t c = sm.cand_keys[j];
+          const uint32_t p = j + lower_rank(cur, int(cnt), c);
+          if (p < bw) nxt[p] = c;
+        }
       }
       cnt = min(bw, cnt + uint32_t(kept));
       uint64_t* t = cur; cur = nxt; nxt = t;
