@@ -190,6 +190,15 @@ int jb_graph_get_directional_flags(int64_t handle, int32_t* out_flags);
  * (include/jasper/rotation/rotation.cuh:74-110). */
 int jb_rotation_matrix(uint32_t dim, uint64_t seed, float* out);
 
+/* Rotate n rows by the prerotation of (dim, seed): out[r] = P^T rows[r]
+ * (reference: rotate_data_vec / the prerotation GEMM, rotation/rotation.cuh:
+ * 122-151, index/construct.cuh:1077-1089).  `rows` and `out` are device
+ * arrays [n][ceil(dim/8)*8] fp16, 16-byte aligned, pad lanes of `rows` zero.
+ * use_tensor_cores = 1 runs the tcgen05 GEMM (the one builds and queries
+ * use), 0 the SIMT reference GEMM.  Synchronous. */
+int jb_rotate_rows(uint32_t dim, uint64_t seed, const uint16_t* rows, uint16_t* out, uint64_t n,
+                   int32_t use_tensor_cores, void* stream);
+
 /* Directional search: kind JB_DIR_LSH (reference: DirectionalSearch_##id ->
  * directional_search, ffi/jasper_ffi_common.cuh:530-609, beam_search/
  * api.cuh:118-138) or JB_DIR_PQ (PqSearch_##id -> pq_search, :611-688,

@@ -72,6 +72,7 @@ SIGNATURES: dict[str, list] = {
                                   C.POINTER(_I64)],
     "jb_graph_get_lsh": [_I64, C.POINTER(_U32), C.POINTER(_U32), _P, _P, _P, C.POINTER(C.c_float)],
     "jb_graph_get_pq": [_I64, C.POINTER(_U32), C.POINTER(_U32), _P, _P, _P],
+    "jb_rotate_rows": [_U32, _U64, _P, _P, _U64, _I32, _P],
 }
 
 

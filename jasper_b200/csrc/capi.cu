@@ -4,9 +4,12 @@
 // a process-wide map from int64 handle to graph, guarded by one mutex that is
 // held only for lookups; the op bodies run unlocked.
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 #include <cstring>
 #include <functional>
 #include <memory>
+#include <tuple>
+#include <map>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -686,6 +689,51 @@ int jb_graph_get_pq(int64_t handle, uint32_t* out_m, uint32_t* out_dsub, float* 
     if (centroids) cuda_check(cudaMemcpy(centroids, d.pq_centroids, size_t(d.pq_m) * 256 * d.pq_dsub * 4, cudaMemcpyDefault), "centroids");
     if (codes) cuda_check(cudaMemcpy(codes, d.pq_codes, size_t(g->n) * g->R * d.pq_m, cudaMemcpyDefault), "codes");
     if (norms && d.norms) cuda_check(cudaMemcpy(norms, d.norms, size_t(g->n) * 4, cudaMemcpyDefault), "norms");
+  });
+}
+
+int jb_rotate_rows(uint32_t dim, uint64_t seed, const uint16_t* rows, uint16_t* out, uint64_t n,
+                   int32_t use_tensor_cores, void* stream) {
+  return guarded([&] {
+    if (dim == 0) throw std::invalid_argument("dim must be > 0");
+    if (n > 0 && (!rows || !out)) throw std::invalid_argument("null argument");
+    if (n == 0) return;
+    const uint32_t dpad = jb::pad_dim(dim);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // The matrix for (device, dim, seed, layout) is built once and kept for
+    // the life of the process (a few hundred KB at most per key).
+    static std::mutex mu;
+    static std::map<std::tuple<int, uint32_t, uint64_t, int>, void*> cache;
+    int dev = 0;
+    cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+    void* dm = nullptr;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      auto key = std::make_tuple(dev, dim, seed, use_tensor_cores ? 1 : 0);
+      auto it = cache.find(key);
+      if (it != cache.end()) {
+        dm = it->second;
+      } else {
+        std::vector<float> P = jb::rotation_matrix_f32(int(dim), seed);
+        std::vector<uint16_t> Ph(P.size());
+        for (size_t i = 0; i < P.size(); i++) {
+          const __half h = __float2half_rn(P[i]);
+          Ph[i] = *reinterpret_cast<const uint16_t*>(&h);
+        }
+        const std::vector<uint16_t> M = use_tensor_cores ? jb::pad_rotation(Ph, dim, dpad) : Ph;
+        cuda_check(cudaMalloc(&dm, M.size() * 2), "alloc rotation");
+        cuda_check(cudaMemcpy(dm, M.data(), M.size() * 2, cudaMemcpyHostToDevice), "rotation");
+        cache[key] = dm;
+      }
+    }
+    if (use_tensor_cores)
+      jb::rotate_rows_tc(static_cast<uint16_t*>(dm), dpad, rows, out, n, st);
+    else
+      jb::rotate_rows(static_cast<uint16_t*>(dm), dim, dpad, rows, out, n, st);
+    cuda_check(cudaStreamSynchronize(st), "rotate");
+    if (use_tensor_cores)
+      if (const int e = jb::rotate_tc_error(true))
+        throw std::runtime_error("rotation GEMM gave up waiting (code " + std::to_string(e) + ")");
   });
 }
 

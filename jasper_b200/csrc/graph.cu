@@ -94,6 +94,7 @@ void graph_free_directional(Graph& g) {
   if (d.pq_codes) cudaFree(d.pq_codes);
   if (d.norms) cudaFree(d.norms);
   if (d.rotation) cudaFree(d.rotation);
+  if (d.rotation_pad) cudaFree(d.rotation_pad);
   d = DirArtifacts{};
 }
 

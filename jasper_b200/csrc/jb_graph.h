@@ -59,6 +59,7 @@ struct DirArtifacts {
   bool prerotate = false;
   uint64_t rotation_seed = 0;
   uint16_t* rotation = nullptr;   // [dim][dim] fp16, column-major P (rows rotate as x^T P)
+  uint16_t* rotation_pad = nullptr;  // [dpad][dpad] fp16, row i = column i of P, zero padded
 };
 
 struct Graph {

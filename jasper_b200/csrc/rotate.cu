@@ -8,7 +8,9 @@
 // algorithm and the same float operation order here, so the matrix is
 // bit-identical under the same standard library.
 //
-// Product: every row x (padded, fp16) becomes y = P^T x, i.e.
+// Product (rotate_rows: a SIMT tiled GEMM kept as the reference for the
+// tensor-core kernel in rotate_tc.cu, which rotate_rows_inplace uses): every
+// row x (padded, fp16) becomes y = P^T x, i.e.
 // y_i = sum_k P[k + i * d] x_k, accumulated in fp32 and rounded to fp16 --
 // the reference's cublasGemmEx(OP_T, OP_N, ...) with fp16 I/O and fp32
 // compute (construct.cuh:1077-1089, rotation.cuh:122-151).  Accumulation
@@ -136,14 +138,30 @@ void check(cudaError_t e, const char* what) {
 
 }  // namespace
 
+std::vector<uint16_t> pad_rotation(const std::vector<uint16_t>& P, uint32_t d, uint32_t dpad) {
+  std::vector<uint16_t> M(size_t(dpad) * dpad, 0);
+  for (uint32_t i = 0; i < d; i++)
+    for (uint32_t k = 0; k < d; k++) M[size_t(i) * dpad + k] = P[k + size_t(i) * d];
+  return M;
+}
+
 void set_rotation(Graph& g, uint64_t seed) {
   std::vector<float> P = rotation_matrix_f32(int(g.dim), seed);
-  std::vector<__half> Ph(P.size());
-  for (size_t i = 0; i < P.size(); i++) Ph[i] = __float2half_rn(P[i]);
+  std::vector<uint16_t> Ph(P.size());
+  for (size_t i = 0; i < P.size(); i++) {
+    const __half h = __float2half_rn(P[i]);
+    Ph[i] = *reinterpret_cast<const uint16_t*>(&h);
+  }
+  const std::vector<uint16_t> Mp = pad_rotation(Ph, g.dim, g.dpad);
   if (g.dir.rotation) cudaFree(g.dir.rotation);
+  if (g.dir.rotation_pad) cudaFree(g.dir.rotation_pad);
   g.dir.rotation = nullptr;
+  g.dir.rotation_pad = nullptr;
   check(cudaMalloc(&g.dir.rotation, Ph.size() * 2), "alloc rotation");
   check(cudaMemcpy(g.dir.rotation, Ph.data(), Ph.size() * 2, cudaMemcpyHostToDevice), "rotation");
+  check(cudaMalloc(&g.dir.rotation_pad, Mp.size() * 2), "alloc padded rotation");
+  check(cudaMemcpy(g.dir.rotation_pad, Mp.data(), Mp.size() * 2, cudaMemcpyHostToDevice),
+        "padded rotation");
   g.dir.prerotate = true;
   g.dir.rotation_seed = seed;
 }
@@ -162,7 +180,15 @@ void rotate_rows_inplace(const Graph& g, uint16_t* rows, uint64_t n, cudaStream_
   if (!g.dir.rotation) throw std::runtime_error("graph has no rotation matrix");
   void* tmp = nullptr;
   check(cudaMallocAsync(&tmp, size_t(n) * g.dpad * 2, st), "alloc rotation scratch");
-  rotate_rows(g.dir.rotation, g.dim, g.dpad, rows, static_cast<uint16_t*>(tmp), n, st);
+  try {
+    rotate_rows_tc(g.dir.rotation_pad, g.dpad, rows, static_cast<uint16_t*>(tmp), n, st);
+    check(cudaStreamSynchronize(st), "rotate");
+    if (const int e = rotate_tc_error(true))
+      throw std::runtime_error("rotation GEMM gave up waiting (code " + std::to_string(e) + ")");
+  } catch (...) {
+    cudaFreeAsync(tmp, st);
+    throw;
+  }
   check(cudaMemcpyAsync(rows, tmp, size_t(n) * g.dpad * 2, cudaMemcpyDeviceToDevice, st),
         "rotated rows");
   check(cudaFreeAsync(tmp, st), "free rotation scratch");

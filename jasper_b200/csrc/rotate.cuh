@@ -16,7 +16,18 @@ void set_rotation(Graph& g, uint64_t seed);
 void rotate_rows(const uint16_t* P, uint32_t d, uint32_t dpad, const uint16_t* X, uint16_t* Y,
                  uint64_t n, cudaStream_t st);
 
-// Rotate n padded rows in place with g's matrix.
+// Tensor-core GEMM (rotate_tc.cu): Y = rows of X times Mp^T, where Mp is the
+// dpad x dpad padded rotation (row i = column i of P).  16-byte aligned
+// buffers; asynchronous on st.
+void rotate_rows_tc(const uint16_t* Mp, uint32_t dpad, const uint16_t* X, uint16_t* Y, uint64_t n,
+                    cudaStream_t st);
+// Error code recorded by a rotate_rows_tc launch whose waits timed out (0 = none).
+int rotate_tc_error(bool reset);
+
+// dpad x dpad padded K-major copy of the column-major d x d matrix P (fp16).
+std::vector<uint16_t> pad_rotation(const std::vector<uint16_t>& P, uint32_t d, uint32_t dpad);
+
+// Rotate n padded rows in place with g's matrix (tensor cores).
 void rotate_rows_inplace(const Graph& g, uint16_t* rows, uint64_t n, cudaStream_t st);
 
 }  // namespace jb

@@ -1,0 +1,336 @@
+// rotate_tc.cu -- prerotation GEMM on the tensor cores (tcgen05, sm_100a).
+//
+// Y[r][i] = sum_k X[r][k] * M[i][k] for every row r, where X holds the rows
+// (fp16, stride dpad, pad lanes zero) and M is the rotation padded to
+// dpad x dpad (row i = output coordinate i, K-contiguous, zeros outside
+// d x d).  This is the reference's cublasGemmEx(OP_T, OP_N) with fp16 I/O and
+// fp32 accumulation (index/construct.cuh:1077-1089, rotation.cuh:122-151);
+// the summation order is the tensor core's, so outputs can differ from cuBLAS
+// in the last fp16 bit.
+//
+// One CTA of 128 threads per 128-row x BN-column output tile:
+//   thread 0     TMA producer: 64-wide K slices of X and M into a ring of
+//                SWIZZLE_128B stages (cp.async.bulk.tensor, no multicast);
+//   thread 32    MMA issuer: per slice four tcgen05.mma kind::f16 (K = 16
+//                each), fp32 accumulator in TMEM; tcgen05.commit frees the
+//                stage and finally signals the epilogue;
+//   all threads  epilogue: tcgen05.ld of the thread's accumulator row (TMEM
+//                lane = output row), round to fp16, store.
+// Every mbarrier wait is bounded: on timeout the CTA records an error code,
+// waits (bounded) for its own bulk copies, frees its TMEM and returns.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdexcept>
+#include <string>
+#include "rotate.cuh"
+
+namespace jb {
+namespace {
+
+constexpr int kBM = 128;          // output rows per CTA (TMEM lanes)
+constexpr int kBK = 64;           // K slice per stage: 64 fp16 = one 128-byte swizzle row
+constexpr uint64_t kWaitNs = 2000000000ull;  // bound on any single wait
+
+__device__ unsigned int g_tc_rotate_error;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase with the given parity.  Bounded: gives up (false) after
+// about two seconds, or as soon as another CTA has recorded an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; it++) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if ((it & 1023) == 0) {
+      const uint64_t now = global_ns();
+      if (it == 0) t0 = now;
+      else if (now - t0 > kWaitNs || *reinterpret_cast<volatile unsigned int*>(&g_tc_rotate_error))
+        return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// K-major SWIZZLE_128B operand: rows of 128 bytes, 8-row groups 1024 bytes
+// apart (SBO), version 1, layout type 2; LBO is unused for this layout (1).
+__device__ __forceinline__ uint64_t sw128_desc(const void* p) {
+  const uint64_t addr = smem_u32(p);
+  return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 accumulator, fp16 A and B, both
+// K-major, M = 128, N = bn.
+__host__ __device__ constexpr uint32_t f16_idesc(uint32_t bn) {
+  return (1u << 4) | ((bn >> 3) << 17) | ((uint32_t(kBM) >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// bn: output columns per CTA (multiple of 16, <= 256); tmem_cols: power of
+// two >= bn; stages: ring depth.
+__global__ void __launch_bounds__(128, 1)
+    rotate_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_m,
+                     uint16_t* __restrict__ Y, uint32_t n, uint32_t dpad, uint32_t bn,
+                     uint32_t tmem_cols, uint32_t stages, uint32_t ksteps) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte aligned stage ring: A slices [stages][128 x 128 B], then B
+  // slices [stages][bn x 128 B]; barriers and the TMEM address after them.
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t a_bytes = kBM * 128, b_bytes = bn * 128;
+  unsigned char* a_ring = base;
+  unsigned char* b_ring = base + size_t(stages) * a_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(b_ring + size_t(stages) * b_bytes);
+  uint64_t* empty = full + stages;
+  uint64_t* done = empty + stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const uint32_t row0 = blockIdx.x * kBM, col0 = blockIdx.y * bn;
+
+  __shared__ uint32_t s_fail;
+  if (tid == 0) {
+    // a CTA that starts after another one failed does nothing
+    s_fail = *reinterpret_cast<volatile unsigned int*>(&g_tc_rotate_error) ? 1u : 0u;
+    for (uint32_t s = 0; s < stages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (s_fail) return;
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (tid == 0) {
+    // producer
+    uint32_t issued = 0;
+    for (uint32_t k = 0; k < ksteps; k++) {
+      const uint32_t s = k % stages;
+      if (k >= stages && !mbar_wait(&empty[s], ((k / stages) - 1) & 1)) {
+        atomicExch(&g_tc_rotate_error, 1u);
+        s_fail = 1;
+        break;
+      }
+      mbar_expect_tx(&full[s], a_bytes + b_bytes);
+      tma_load_2d(a_ring + size_t(s) * a_bytes, &map_x, &full[s], int(k * kBK), int(row0));
+      tma_load_2d(b_ring + size_t(s) * b_bytes, &map_m, &full[s], int(k * kBK), int(col0));
+      issued++;
+    }
+    // drain: every issued copy has landed before the CTA can leave
+    for (uint32_t k = (issued > stages ? issued - stages : 0); k < issued; k++)
+      if (!mbar_wait(&full[k % stages], (k / stages) & 1)) atomicExch(&g_tc_rotate_error, 2u);
+  } else if (tid == 32) {
+    // MMA issuer
+    const uint32_t idesc = f16_idesc(bn);
+    bool ok = true;
+    for (uint32_t k = 0; k < ksteps; k++) {
+      const uint32_t s = k % stages;
+      if (!mbar_wait(&full[s], (k / stages) & 1)) {
+        atomicExch(&g_tc_rotate_error, 3u);
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint64_t ad = sw128_desc(a_ring + size_t(s) * a_bytes);
+      const uint64_t bd = sw128_desc(b_ring + size_t(s) * b_bytes);
+#pragma unroll
+      for (int kk = 0; kk < kBK / 16; kk++)  // 32 bytes of K per MMA: +2 in the address field
+        mma_f16(tmem, ad + 2ull * kk, bd + 2ull * kk, idesc, (k | kk) ? 1u : 0u);
+      mma_commit(&empty[s]);
+    }
+    if (!ok) s_fail = 1;
+    mma_commit(done);  // arrives once every MMA issued above has completed
+  }
+  __syncwarp();
+  // epilogue (all 128 threads): thread t owns TMEM lane t = output row row0 + t
+  int failed = (tid == 0 || tid == 32) ? int(s_fail) : 0;
+  if (!mbar_wait(done, 0)) {
+    atomicExch(&g_tc_rotate_error, 4u);
+    failed = 1;
+  }
+  // CTA-uniform decision: tcgen05.ld below is warp-collective
+  failed = __syncthreads_or(failed);
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (!failed) {
+    const uint32_t r = row0 + uint32_t(tid);
+    const uint32_t lane_base = uint32_t(warp * 32) << 16;
+    for (uint32_t c = 0; c < bn; c += 16) {
+      uint32_t v[16];
+      tmem_ld16(tmem + lane_base + c, v);
+      if (r < n && col0 + c < dpad) {
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const __half2 h2 = __floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+          w[j] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        uint16_t* dst = Y + size_t(r) * dpad + col0 + c;
+        if (col0 + c + 16 <= dpad) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst);
+          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        } else {
+#pragma unroll
+          for (uint32_t j = 0; j < 16; j++)
+            if (col0 + c + j < dpad) dst[j] = uint16_t(w[j >> 1] >> (16 * (j & 1)));
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(tmem_cols)
+                 : "memory");
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || p == nullptr)
+      throw std::runtime_error("cuTensorMapEncodeTiled is not available");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D fp16 map over rows x cols (row stride `stride` elements), box of
+// box_rows x 64 with 128-byte swizzle; out-of-range elements read as zero.
+CUtensorMap make_map(const void* ptr, uint64_t rows, uint64_t cols, uint64_t stride,
+                     uint32_t box_rows) {
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {stride * 2};
+  const cuuint32_t box[2] = {uint32_t(kBK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr),
+                                 dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return m;
+}
+
+}  // namespace
+
+void rotate_rows_tc(const uint16_t* Mp, uint32_t dpad, const uint16_t* X, uint16_t* Y, uint64_t n,
+                    cudaStream_t st) {
+  if (n == 0) return;
+  if (dpad % 8 != 0 || dpad == 0) throw std::invalid_argument("rotate: dpad must be a multiple of 8");
+  if (n >= (uint64_t(1) << 31)) throw std::invalid_argument("rotate: too many rows");
+  if ((reinterpret_cast<uintptr_t>(X) | reinterpret_cast<uintptr_t>(Y) |
+       reinterpret_cast<uintptr_t>(Mp)) % 16)
+    throw std::invalid_argument("rotate: buffers must be 16-byte aligned");
+  // N tiles of at most 256 columns (multiple of 16)
+  const uint32_t ntiles = (dpad + 255) / 256;
+  uint32_t bn = (dpad + ntiles - 1) / ntiles;
+  bn = (bn + 15) / 16 * 16;
+  uint32_t tmem_cols = 32;
+  while (tmem_cols < bn) tmem_cols <<= 1;
+  const uint32_t ksteps = (dpad + kBK - 1) / kBK;
+  const size_t stage_bytes = size_t(kBM) * 128 + size_t(bn) * 128;
+  uint32_t stages = ksteps < 4 ? ksteps : 4;
+  while (stages > 1 && stages * stage_bytes + 2048 > 200 * 1024) stages--;
+  const size_t smem = stages * stage_bytes + 1024 /* alignment */ + 8 * (2 * stages + 1) + 16;
+  const CUtensorMap mx = make_map(X, n, dpad, dpad, kBM);
+  const CUtensorMap mm = make_map(Mp, dpad, dpad, dpad, bn);
+  cudaFuncSetAttribute(rotate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  const dim3 grid(uint32_t((n + kBM - 1) / kBM), (dpad + bn - 1) / bn);
+  rotate_tc_kernel<<<grid, 128, smem, st>>>(mx, mm, Y, uint32_t(n), dpad, bn, tmem_cols, stages,
+                                            ksteps);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("rotate launch: ") + cudaGetErrorString(e));
+}
+
+int rotate_tc_error(bool reset) {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_rotate_error, sizeof(v));
+  if (reset) {
+    const unsigned int z = 0;
+    cudaMemcpyToSymbol(g_tc_rotate_error, &z, sizeof(z));
+  }
+  return int(v);
+}
+
+}  // namespace jb

@@ -45,3 +45,42 @@ def test_r_diagonal_sign_convention():
     d, seed = 24, 11
     P = rot(d, seed).astype(np.float64)
     assert np.isfinite(P).all()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dim,n", [(128, 20000), (96, 3000), (200, 5000), (960, 2000), (40, 700)])
+def test_tensor_core_rotation_matches_reference_gemm(cuda, dim, n):
+    """tcgen05 rotation GEMM vs the SIMT fp32-accumulate GEMM and a float64
+    product of the same fp16 operands.  Tolerance per output: 1 fp16 ulp of
+    the exact value (final rounding) plus the fp32 summation bound
+    dim * 2^-24 * sum_k |x_k a_k| (the two GEMMs only sum in different
+    orders)."""
+    import torch
+    from jasper_b200 import _lib
+    rng = np.random.default_rng(dim)
+    dpad = (dim + 7) // 8 * 8
+    X = np.zeros((n, dpad), np.float16)
+    X[:, :dim] = rng.standard_normal((n, dim)).astype(np.float16)
+    x = torch.from_numpy(X.view(np.uint16)).cuda()
+    outs = []
+    for tc in (1, 0):
+        y = torch.full((n, dpad), 0x7E00, dtype=torch.int16, device="cuda")
+        _lib.call("jb_rotate_rows", dim, 7, x.data_ptr(), y.data_ptr(), n, tc,
+                  torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        outs.append(y.cpu().numpy().view(np.float16).astype(np.float64))
+    Yt, Ys = outs
+    P = np.zeros((dim, dim), np.float32)
+    _lib.call("jb_rotation_matrix", dim, 7, P.ctypes.data)
+    A = P.astype(np.float16).astype(np.float64)      # row i = weights of output i
+    Xd = X[:, :dim].astype(np.float64)
+    exact = Xd @ A.T
+    tol = (np.spacing(np.abs(exact).astype(np.float16)).astype(np.float64)
+           + dim * 2.0 ** -24 * (np.abs(Xd) @ np.abs(A).T))
+    for name, Y in (("tensor cores", Yt), ("simt", Ys)):
+        err = np.abs(Y[:, :dim] - exact)
+        bad = err > tol
+        r, c = np.nonzero(bad)
+        assert not bad.any(), (name, int(bad.sum()), r[:5], c[:5], err[bad][:5], tol[bad][:5])
+    assert np.all(Yt[:, dim:] == 0)                    # pad lanes stay zero
+    assert (Yt == Ys).mean() > 0.98
