@@ -40,6 +40,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 BWS = (16, 32, 64, 128, 256)
+# DRAM bytes (read + write) of one search launch, from an ncu capture of this
+# bench's own launch: (rows, queries, beam width) -> bytes.
+SEARCH_TRAFFIC = {(1_000_000, 10_000, 32): 1_374_990_640}
 TARGET = 0.95
 K = 10
 METRIC = "QPS at recall@10=0.95 and build Mvec/s, 1M×128 fp16, at 1/2/4/8 B200"
@@ -290,8 +293,12 @@ def run_jasper(args):
     bytes_q = (2 * dpad + st[:, 0] + 4 * st[:, 1] + 2 * dpad * st[:, 4] + 8 * K).sum().item()
     peak, peak_kind = measured_peaks()
     achieved = bytes_q / (ms[hi] / 1e3) / 1e9
+    traffic = SEARCH_TRAFFIC.get((args.n, args.nq, hi))
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": None,
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "traffic_source": "profiles/search_cfg2_bw32.md (dram__bytes_read.sum + "
+                                  "dram__bytes_write.sum, one launch)" if traffic else None,
+                "algorithmic_bytes_per_launch": int(bytes_q),
                 "peak_source": peak_kind, "kernel": f"beam_search_warp_kernel bw={hi}",
                 "bytes_per_query": round(bytes_q / args.nq, 1),
                 "expansions_per_query": round(st[:, 0].float().mean().item(), 2),
@@ -496,9 +503,11 @@ def run_sharded(args):
     # e2e: queries from pinned host memory, the merged top-k back to the host
     q_host = queries.cpu().pin_memory()
     e2e = {}
+    clk_e2e = ClockSampler(dev)
+    clk_e2e.__enter__()
     for bw in pair:
         ts = []
-        for _ in range(max(args.steps, 5)):
+        for it in range(max(args.steps, 10) + args.warmup):
             barrier()
             t1 = time.perf_counter()
             qd = q_host.to(dev, non_blocking=True)
@@ -507,8 +516,10 @@ def run_sharded(args):
             if res is not None:
                 res[0].cpu(), res[1].cpu()
             torch.cuda.synchronize()
-            ts.append(time.perf_counter() - t1)
+            if it >= args.warmup:
+                ts.append(time.perf_counter() - t1)
         e2e[bw] = float(np.median(ts)) * 1e3
+    clk_e2e.__exit__(None, None, None)
     e2e = dict(zip(pair, max_over_ranks([e2e[bw] for bw in pair])))
     e2e_qps = {bw: args.nq / (e2e[bw] / 1e3) for bw in pair}
     e2e_value = interp_qps(recalls[lo], e2e_qps[lo], recalls[hi], e2e_qps[hi])
@@ -533,7 +544,10 @@ def run_sharded(args):
                       "note": f"{ws} shards built concurrently; time = max over ranks"},
             "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
                     "h2d_bytes_per_step": int(len(pair) * args.nq * 128 * 2),
-                    "d2h_bytes_per_step": int(len(pair) * args.nq * K * 8)},
+                    "d2h_bytes_per_step": int(len(pair) * args.nq * K * 8),
+                    "timing": "median host wall time per query batch (upload, search on "
+                              "every shard, gather, merge, download), max over ranks",
+                    "clocks": clk_e2e.summary()},
             "gpu_launches": args.steps * len(pair) * (2 if ws > 1 else 1),
             "clocks": clk.summary(),
         }
@@ -541,6 +555,48 @@ def run_sharded(args):
     sg.free()
     if dist is not None:
         dist.destroy_process_group()
+
+
+# ── prerotation GEMM (tensor cores vs the SIMT reference GEMM) ───────────
+def run_rotation(args):
+    """Times jb_rotate_rows (Y = rows x P^T, fp16 in/out, fp32 accumulation)
+    on the tcgen05 kernel and on the SIMT GEMM at the config-3 (D = 128,
+    1M rows) and config-4 (D = 960, 250k rows) shapes; one JSON line each."""
+    from jasper_b200 import _lib
+    torch.cuda.set_device(0)
+    peak_tf = 1657.0
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        peak_tf = float(json.loads(p.read_text()).get("bf16_tflops", peak_tf))
+    hbm, _ = measured_peaks()
+    for dim, n in ((128, 1_000_000), (960, 250_000)):
+        dpad = (dim + 7) // 8 * 8
+        g = torch.Generator(device="cuda").manual_seed(4)
+        x = torch.randn(n, dpad, generator=g, device="cuda").half()
+        y = torch.empty_like(x)
+        line = {"mode": "rotation", "dim": dim, "rows": n}
+        for tc in (1, 0):
+            for _ in range(args.warmup):
+                _lib.call("jb_rotate_rows", dim, 4, x.data_ptr(), y.data_ptr(), n, tc,
+                          torch.cuda.current_stream().cuda_stream)
+            ts = []
+            for _ in range(args.steps):
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                _lib.call("jb_rotate_rows", dim, 4, x.data_ptr(), y.data_ptr(), n, tc,
+                          torch.cuda.current_stream().cuda_stream)
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            ms = float(np.median(ts))
+            tflops = 2.0 * n * dpad * dpad / ms / 1e9
+            gbs = (4.0 * n * dpad + 2.0 * dpad * dpad) / ms / 1e6
+            line["tcgen05" if tc else "simt"] = {
+                "ms": round(ms, 4), "tflops": round(tflops, 1), "gbs": round(gbs, 1),
+                "frac_of_bf16_peak": round(tflops / peak_tf, 4),
+                "frac_of_hbm": round(gbs / hbm, 4)}
+        print(json.dumps(line), flush=True)
 
 
 # ── reference arm ─────────────────────────────────────────────────────────
@@ -631,8 +687,9 @@ def main():
     ap.add_argument("--nq", type=int, default=10_000)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", default="replicas", choices=["replicas", "sharded"],
-                    help="replicas: config 2 per GPU (default); sharded: config 5 range shards")
+    ap.add_argument("--mode", default="replicas", choices=["replicas", "sharded", "rotation"],
+                    help="replicas: config 2 per GPU (default); sharded: config 5 range "
+                         "shards; rotation: the prerotation GEMM alone")
     ap.add_argument("--n-shard", type=int, default=12_500_000,
                     help="rows per GPU in --mode sharded (config 5: 12.5M)")
     args = ap.parse_args()
@@ -642,6 +699,8 @@ def main():
         run_reference(args)
     elif args.mode == "sharded":
         run_sharded(args)
+    elif args.mode == "rotation":
+        run_rotation(args)
     else:
         run_jasper(args)
 
