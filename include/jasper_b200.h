@@ -164,6 +164,7 @@ int jb_graph_apply_global_offset(int64_t handle, uint32_t offset);
 
 #define JB_DIR_LSH 0
 #define JB_DIR_PQ 1
+#define JB_DIR_RABITQ 2
 
 /* Attach cross-polytope LSH edge payloads (host arrays): packed [n][R *
  * k_ranks] words of packed_bytes (1: 7-bit coord, 2: 15-bit coord; sign in
@@ -181,7 +182,7 @@ int jb_graph_set_lsh(int64_t handle, uint32_t k_ranks, uint32_t packed_bytes, co
 int jb_graph_set_pq(int64_t handle, uint32_t m, uint32_t dsub, const float* centroids,
                     const uint8_t* codes, const float* norms);
 
-/* Which payloads a graph carries: bit 0 LSH, bit 1 PQ (reference:
+/* Which payloads a graph carries: bit 0 LSH, bit 1 PQ, bit 2 RaBitQ (reference:
  * jasper_get_directional_flags_<cfg>, ffi/jasper_ffi_common.cuh:760-775). */
 int jb_graph_get_directional_flags(int64_t handle, int32_t* out_flags);
 
@@ -260,6 +261,31 @@ int jb_graph_get_lsh(int64_t handle, uint32_t* out_k_ranks, uint32_t* out_packed
  * Any output pointer may be NULL to skip it.  Synchronous. */
 int jb_graph_get_pq(int64_t handle, uint32_t* out_m, uint32_t* out_dsub, float* centroids,
                     uint8_t* codes, float* norms);
+
+/* ── RaBitQ (1 bit per dimension) ────────────────────────────────────── */
+
+/* The reference's quantizer rabitq_quantize<1> (include/jasper/rabitq/
+ * quantize.cuh:296-353): rows [n][dim] f32, rotation (dim x dim f32
+ * column-major; NULL = identity; rows are rotated by P^T and the centroid by
+ * P, as the reference does), centroid [dim] f32, metric -> out: n nodes of
+ * ceil(dim/8) code bytes padded to 4, then f_add and f_rescale (f32)
+ * (rabitq/layout.cuh:42-116).  Device pointers; asynchronous on `stream`. */
+int jb_rabitq_quantize(const float* rows, uint64_t n, uint32_t dim, const float* rotation,
+                       const float* centroid, int32_t metric, uint8_t* out, void* stream);
+
+/* RaBitQ codes of the graph's own rows (prerotated when the graph was built
+ * with prerotation) around their column mean; enables
+ * jb_graph_directional_search(kind = JB_DIR_RABITQ).  No reference
+ * counterpart: the reference quantizes but has no RaBitQ search.
+ * Synchronous. */
+int jb_graph_build_rabitq(int64_t handle);
+
+/* Attach / read RaBitQ payloads (host arrays): store [n][node_bytes] as
+ * jb_rabitq_quantize writes it, centroid [dim] f32.  Either output pointer
+ * of the getter may be NULL. */
+int jb_graph_set_rabitq(int64_t handle, uint32_t node_bytes, const uint8_t* store,
+                        const float* centroid);
+int jb_graph_get_rabitq(int64_t handle, uint32_t* out_node_bytes, uint8_t* store, float* centroid);
 
 /* Merge per-shard top-k lists (device pointers, [n_shards][n_queries][k])
  * into the global top-k by (distance, id), on `stream`.  Used after the shards

@@ -116,6 +116,7 @@ class Graph:
         self._has_pq = has_pq
         self._prerotate = prerotate
         self._prerotate_seed = prerotate_seed
+        self._has_rabitq = False
 
     # ── construction / persistence ─────────────────────────────────────
     @classmethod
@@ -159,8 +160,14 @@ class Graph:
               workspace_budget: str = "10GB", on_host: bool = False, build_lsh: bool = False,
               build_pq: bool = False, k_ranks: int = 4, prerotate: bool | None = None,
               prerotate_seed: int = 42, lsh_samples: int = 32768, lsh_seed: int = 42,
-              pq_train: int = 40000, pq_kmeans_iter: int = 12, pq_seed: int = 123) -> "Graph":
-        """Construct a graph from [n, dim] float16 vectors (CUDA or host tensor)."""
+              pq_train: int = 40000, pq_kmeans_iter: int = 12, pq_seed: int = 123,
+              build_rabitq: bool = False) -> "Graph":
+        """Construct a graph from [n, dim] float16 vectors (CUDA or host tensor).
+
+        ``build_lsh`` / ``build_pq`` / ``build_rabitq`` build a directional
+        graph (prerotated unless ``prerotate=False``) with the corresponding
+        estimator payloads; ``build_rabitq`` (1-bit RaBitQ codes of the rows,
+        an addition of this package) enables :meth:`rabitq_search`."""
         distance = DistanceFunc(distance)
         budget = parse_storage_size(workspace_budget)
         if vectors.ndim != 2:
@@ -173,7 +180,7 @@ class Graph:
         stream = _stream_ptr(vectors.device) if vectors.is_cuda else 0
         if vectors.is_cuda:
             torch.cuda.set_device(vectors.device)
-        if not (build_lsh or build_pq):
+        if not (build_lsh or build_pq or build_rabitq):
             config_id = _resolve_config(DataType.FLOAT16, n_neighbors, distance)
             _lib.call("jb_graph_construct", _ptr(vectors), n, dim, dim, n_neighbors,
                       _METRIC[distance], float(alpha), budget, int(on_host), stream, C.byref(h))
@@ -192,6 +199,9 @@ class Graph:
         if build_pq:
             _lib.call("jb_graph_build_pq", h.value, int(k_ranks), int(pq_train),
                       int(pq_kmeans_iter), int(pq_seed))
+        if build_rabitq:
+            _lib.call("jb_graph_build_rabitq", h.value)
+            g._has_rabitq = True
         return g
 
     # ── properties ─────────────────────────────────────────────────────
@@ -334,6 +344,17 @@ class Graph:
             raise RuntimeError("pq_search() requires a graph built with build_pq=True "
                                "(or loaded with PQ artifacts present)")
         return self._dir_search(1, "pq_search", queries, k, beam_width, limit, print_throughput)
+
+    def rabitq_search(self, queries: torch.Tensor, k: int = 10, beam_width: int = 128,
+                      limit: int | None = None, print_throughput: bool = False):
+        """Beam search scored by the RaBitQ 1-bit estimator (codes built with
+        ``build_rabitq=True``): candidates are ranked by the estimate, every
+        expanded node by its exact distance (the directional search loop).
+        Returns (int32 [nq, k] ids, float32 [nq, k] exact distances)."""
+        self._check_alive()
+        if not self._is_directional or not self._has_rabitq:
+            raise RuntimeError("rabitq_search() requires a graph built with build_rabitq=True")
+        return self._dir_search(2, "rabitq_search", queries, k, beam_width, limit, print_throughput)
 
     # ── rows, ids, deletion ───────────────────────────────────────────
     def get_vector(self, stable_id: int) -> torch.Tensor:

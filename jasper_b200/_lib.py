@@ -73,6 +73,10 @@ SIGNATURES: dict[str, list] = {
     "jb_graph_get_lsh": [_I64, C.POINTER(_U32), C.POINTER(_U32), _P, _P, _P, C.POINTER(C.c_float)],
     "jb_graph_get_pq": [_I64, C.POINTER(_U32), C.POINTER(_U32), _P, _P, _P],
     "jb_rotate_rows": [_U32, _U64, _P, _P, _U64, _I32, _P],
+    "jb_rabitq_quantize": [_P, _U64, _U32, _P, _P, _I32, _P, _P],
+    "jb_graph_build_rabitq": [_I64],
+    "jb_graph_set_rabitq": [_I64, _U32, _P, _P],
+    "jb_graph_get_rabitq": [_I64, C.POINTER(_U32), _P, _P],
 }
 
 

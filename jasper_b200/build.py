@@ -21,7 +21,7 @@ OBJ = PKG / "lib" / "obj"
 ROOT = PKG.parent
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CORE_SOURCES = ["search.cu", "construct.cu", "graph.cu", "merge.cu", "capi.cu", "noalloc.cu", "dirsearch.cu", "rotate.cu", "rotate_tc.cu", "builders.cu"]
+CORE_SOURCES = ["search.cu", "construct.cu", "graph.cu", "merge.cu", "capi.cu", "noalloc.cu", "dirsearch.cu", "rotate.cu", "rotate_tc.cu", "builders.cu", "rabitq.cu"]
 COMMON_FLAGS = ["-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
                 "-I" + str(ROOT / "include")]
 

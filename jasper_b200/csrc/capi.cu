@@ -17,6 +17,7 @@
 #include <vector>
 #include "../../include/jasper_b200.h"
 #include "builders.cuh"
+#include "rabitq.cuh"
 #include "construct.cuh"
 #include "dirsearch.cuh"
 #include "rotate.cuh"
@@ -493,7 +494,7 @@ int jb_graph_get_directional_flags(int64_t handle, int32_t* out_flags) {
   return guarded([&] {
     if (!out_flags) throw std::invalid_argument("out_flags is null");
     auto g = lookup(handle);
-    *out_flags = (g->dir.has_lsh ? 1 : 0) | (g->dir.has_pq ? 2 : 0);
+    *out_flags = (g->dir.has_lsh ? 1 : 0) | (g->dir.has_pq ? 2 : 0) | (g->dir.has_rabitq ? 4 : 0);
   });
 }
 
@@ -504,12 +505,15 @@ int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* qu
   return guarded([&] {
     auto g = lookup(handle);
     DeviceScope ds(g->device);
-    if (kind != JB_DIR_LSH && kind != JB_DIR_PQ) throw std::invalid_argument("kind must be LSH or PQ");
+    if (kind != JB_DIR_LSH && kind != JB_DIR_PQ && kind != JB_DIR_RABITQ)
+      throw std::invalid_argument("kind must be LSH, PQ or RaBitQ");
     const jb::DirArtifacts& d = g->dir;
     if (kind == JB_DIR_LSH && !d.has_lsh)
       throw std::runtime_error("Graph " + std::to_string(handle) + " has no LSH artifacts built");
     if (kind == JB_DIR_PQ && !d.has_pq)
       throw std::runtime_error("Graph " + std::to_string(handle) + " has no PQ artifacts built");
+    if (kind == JB_DIR_RABITQ && !d.has_rabitq)
+      throw std::runtime_error("Graph " + std::to_string(handle) + " has no RaBitQ codes built");
     if (n_queries == 0) return;
     if (!queries || !out_idx || !out_dist) throw std::invalid_argument("null pointer argument");
     if (row_stride < g->dim) throw std::invalid_argument("row_stride < dim");
@@ -544,6 +548,10 @@ int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* qu
     a.centroids = d.pq_centroids;
     a.codes = d.pq_codes;
     a.norms = d.norms;
+    a.rq_store = d.rq_store;
+    a.rq_node_bytes = d.rq_node_bytes;
+    a.rq_code_bytes = d.rq_code_bytes;
+    a.rq_centroid = d.rq_centroid;
     a.queries = q;
     a.nq = uint32_t(n_queries);
     a.k = k;
@@ -734,6 +742,61 @@ int jb_rotate_rows(uint32_t dim, uint64_t seed, const uint16_t* rows, uint16_t* 
     if (use_tensor_cores)
       if (const int e = jb::rotate_tc_error(true))
         throw std::runtime_error("rotation GEMM gave up waiting (code " + std::to_string(e) + ")");
+  });
+}
+
+int jb_rabitq_quantize(const float* rows, uint64_t n, uint32_t dim, const float* rotation,
+                       const float* centroid, int32_t metric, uint8_t* out, void* stream) {
+  return guarded([&] {
+    check_metric(metric);
+    if (n > 0 && (!rows || !centroid || !out)) throw std::invalid_argument("null argument");
+    jb::rabitq_quantize_rows(rows, n, dim, rotation, centroid, metric == JB_METRIC_IP ? 1 : 0, out,
+                             static_cast<cudaStream_t>(stream));
+  });
+}
+
+int jb_graph_build_rabitq(int64_t handle) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    cuda_check(cudaDeviceSynchronize(), "sync before build_rabitq");
+    jb::build_rabitq(*g, nullptr);
+  });
+}
+
+int jb_graph_set_rabitq(int64_t handle, uint32_t node_bytes, const uint8_t* store,
+                        const float* centroid) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    const uint32_t cb = jb::rabitq_code_bytes(g->dim);
+    if (node_bytes != cb + 8)
+      throw std::invalid_argument("node_bytes must be " + std::to_string(cb + 8) + " for dim " +
+                                  std::to_string(g->dim));
+    if (!store || !centroid) throw std::invalid_argument("null argument");
+    jb::DirArtifacts& d = g->dir;
+    if (d.rq_store) { cudaFree(d.rq_store); d.rq_store = nullptr; }
+    if (d.rq_centroid) { cudaFree(d.rq_centroid); d.rq_centroid = nullptr; }
+    cuda_check(cudaMalloc(&d.rq_store, size_t(g->n) * node_bytes + 16), "alloc rabitq codes");
+    cuda_check(cudaMalloc(&d.rq_centroid, size_t(g->dim) * 4 + 16), "alloc rabitq centroid");
+    cuda_check(cudaMemcpy(d.rq_store, store, size_t(g->n) * node_bytes, cudaMemcpyDefault), "codes");
+    cuda_check(cudaMemcpy(d.rq_centroid, centroid, size_t(g->dim) * 4, cudaMemcpyDefault), "centroid");
+    d.rq_code_bytes = cb;
+    d.rq_node_bytes = node_bytes;
+    d.has_rabitq = true;
+  });
+}
+
+int jb_graph_get_rabitq(int64_t handle, uint32_t* out_node_bytes, uint8_t* store, float* centroid) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    const jb::DirArtifacts& d = g->dir;
+    if (!d.has_rabitq) throw std::runtime_error("Graph " + std::to_string(handle) + " has no RaBitQ codes built");
+    cuda_check(cudaDeviceSynchronize(), "sync");
+    if (out_node_bytes) *out_node_bytes = d.rq_node_bytes;
+    if (store) cuda_check(cudaMemcpy(store, d.rq_store, size_t(g->n) * d.rq_node_bytes, cudaMemcpyDefault), "codes");
+    if (centroid) cuda_check(cudaMemcpy(centroid, d.rq_centroid, size_t(g->dim) * 4, cudaMemcpyDefault), "centroid");
   });
 }
 

@@ -95,6 +95,8 @@ void graph_free_directional(Graph& g) {
   if (d.norms) cudaFree(d.norms);
   if (d.rotation) cudaFree(d.rotation);
   if (d.rotation_pad) cudaFree(d.rotation_pad);
+  if (d.rq_store) cudaFree(d.rq_store);
+  if (d.rq_centroid) cudaFree(d.rq_centroid);
   d = DirArtifacts{};
 }
 

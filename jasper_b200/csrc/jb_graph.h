@@ -56,6 +56,10 @@ struct DirArtifacts {
   float* pq_centroids = nullptr;  // [M][256][dsub]
   uint8_t* pq_codes = nullptr;    // [n][M * R], code of edge e in subspace j at j * R + e
   float* norms = nullptr;         // [n] exact |x|^2
+  bool has_rabitq = false;
+  uint32_t rq_code_bytes = 0, rq_node_bytes = 0;
+  uint8_t* rq_store = nullptr;    // [n][rq_node_bytes]: code bits, f_add, f_rescale (f32)
+  float* rq_centroid = nullptr;   // [dim] column mean of the rows the codes were made from
   bool prerotate = false;
   uint64_t rotation_seed = 0;
   uint16_t* rotation = nullptr;   // [dim][dim] fp16, column-major P (rows rotate as x^T P)

@@ -37,3 +37,11 @@ g++ -shared -o "$OUT/lib/libjasper_ffi.so" $objs "$OUT/obj/dlink.o" \
   -L/usr/local/cuda/lib64 -lcudart -lcublas -lcurand \
   -L$TVM/lib -ltvm_ffi -Wl,-rpath,$TVM/lib -Wl,-rpath,/usr/local/cuda/lib64
 echo "built $OUT/lib/libjasper_ffi.so"
+# RaBitQ quantizer driver (header-only reference code; our main() in
+# oracle/ref_rabitq_driver.cu)
+mkdir -p "$OUT/bin"
+if [ ! -f "$OUT/bin/ref_rabitq" ] || [ "$HERE/ref_rabitq_driver.cu" -nt "$OUT/bin/ref_rabitq" ]; then
+  nvcc -std=c++17 -O3 -gencode arch=compute_100a,code=sm_100a -lineinfo --expt-relaxed-constexpr \
+    -I$REF/include "$HERE/ref_rabitq_driver.cu" -o "$OUT/bin/ref_rabitq" -lcublas -lcurand
+fi
+echo "built $OUT/bin/ref_rabitq"

@@ -647,6 +647,9 @@ typedef struct {
   const float *centroids;   /* [M][256][dsub] */
   const uint8_t *codes;     /* [n][M * R] subspace-major */
   const float *norms;       /* [n] */
+  const uint8_t *rq_store;  /* RaBitQ: [n][node_bytes] {code bits, f_add, f_rescale} */
+  uint32_t rq_node_bytes, rq_code_bytes;
+  const float *rq_centroid; /* [dim], rotated space */
 } orc_dir;
 
 /* compute_qu_diff_and_exact (beam_search_common.cuh:87-154); fills qu (fp16
@@ -700,6 +703,149 @@ static void fr_insert(orc_entry *fr, uint32_t *fc, uint32_t k, uint32_t idx, flo
   fr[j].idx = idx; fr[j].dist = d;
 }
 
+/* ---- RaBitQ (1 bit per dimension) ------------------------------------- */
+
+/* Query side of the RaBitQ estimator (no reference counterpart; the device
+ * kernel computes the same values in the same order).  q = fp16 query in the
+ * rotated space, first `dim` coordinates:
+ *   vl = min q_i, delta = (max q_i - vl) / 15, qq_i = clamp(rint((q_i - vl) *
+ *   15 / (max - vl)), 0, 15), S = sum qq_i, plane p bit i = (qq_i >> p) & 1;
+ *   gadd = sum (q_i - c_i)^2 (L2) or -sum c_i q_i (IP), summed lane-strided
+ *   over 32 lanes (i = l, l + 32, ...; fma) and reduced by the warp butterfly. */
+static void rabitq_query_prep(const uint16_t *q, uint32_t dim, const float *c, int ip,
+                              uint32_t *planes, float *vl_out, float *delta_out, int *S_out,
+                              float *gadd_out) {
+  float vl = orc_half_to_float(q[0]), vr = vl;
+  for (uint32_t i = 1; i < dim; i++) {
+    float x = orc_half_to_float(q[i]);
+    if (x < vl) vl = x;
+    if (x > vr) vr = x;
+  }
+  const float range = vr - vl;
+  const float delta = range / 15.0f;
+  const float inv = range > 0.0f ? 15.0f / range : 0.0f;
+  int S = 0;
+  for (uint32_t i = 0; i < dim; i++) {
+    float x = orc_half_to_float(q[i]);
+    int qq = (int)rintf((x - vl) * inv);
+    if (qq < 0) qq = 0;
+    if (qq > 15) qq = 15;
+    S += qq;
+    for (int p = 0; p < 4; p++)
+      if ((qq >> p) & 1) planes[(size_t)p * ((dim + 31) / 32) + i / 32] |= 1u << (i % 32);
+  }
+  float v[32];
+  for (int l = 0; l < 32; l++) {
+    float acc = 0.f;
+    for (uint32_t i = (uint32_t)l; i < dim; i += 32) {
+      float x = orc_half_to_float(q[i]);
+      if (ip) acc = fmaf(c[i], x, acc);
+      else { float d = x - c[i]; acc = fmaf(d, d, acc); }
+    }
+    v[l] = acc;
+  }
+  float gsum = warp_reduce32(v);
+  *vl_out = vl; *delta_out = delta; *S_out = S;
+  *gadd_out = ip ? -gsum : gsum;
+}
+
+/* est = f_add + f_rescale * <code - 1/2, q~> + gadd (IP: minus 1, the
+ * distance being -<o, q> while f_add carries 1 - <o, q>), with
+ * <code - 1/2, q~> = 0.5 vl (2 popc(b) - dim) + 0.5 delta (2 A - S) and
+ * A = sum_p 2^p popc(b & plane_p). */
+static float rabitq_estimate(const uint8_t *node, uint32_t code_bytes, uint32_t dim,
+                             const uint32_t *planes, float vl, float delta, int S, float gadd,
+                             int ip) {
+  const uint32_t nw = (dim + 31) / 32;
+  int A = 0, pb = 0;
+  for (uint32_t w = 0; w < nw; w++) {
+    uint32_t b;
+    memcpy(&b, node + 4 * w, 4);
+    pb += __builtin_popcount(b);
+    for (int p = 0; p < 4; p++) A += __builtin_popcount(b & planes[(size_t)p * nw + w]) << p;
+  }
+  float f_add, f_rescale;
+  memcpy(&f_add, node + code_bytes, 4);
+  memcpy(&f_rescale, node + code_bytes + 4, 4);
+  const float t1 = (float)(2 * pb - (int)dim) * (0.5f * vl);
+  const float ipx = fmaf((float)(2 * A - S), 0.5f * delta, t1);
+  float est = fmaf(f_rescale, ipx, f_add) + gadd;
+  return ip ? est - 1.0f : est;
+}
+
+/* rabitq_quantize_kernel<1, TILE_SIZE = 4> (rabitq/quantize.cuh:184-290) for
+ * every row of `rows` ([n][stride] floats, first `dim` used): residual
+ * r = x - c, partial sums by thread j % 4 with fma, the tile's xor-butterfly
+ * (mask 2 then 1); code bit = r >= 0; f_add / f_rescale as the reference
+ * writes them.  Output: the reference's array-of-structs node layout. */
+static void rabitq_row(const float *x, const float *c, uint32_t dim, int ip, uint8_t *node,
+                       uint32_t code_bytes) {
+  float part[4] = {0, 0, 0, 0};
+  for (uint32_t j = 0; j < dim; j++) { float r = x[j] - c[j]; part[j % 4] = fmaf(r, r, part[j % 4]); }
+  const float l2_sqr = (part[0] + part[2]) + (part[1] + part[3]);
+  const float l2_norm = sqrtf(l2_sqr);
+  float pn[4] = {0, 0, 0, 0};
+  for (uint32_t j = 0; j < dim; j++) {
+    float r = x[j] - c[j];
+    float abs_o = fabsf(r / l2_norm);
+    pn[j % 4] = fmaf(0.5f, abs_o, pn[j % 4]);
+  }
+  const float ip_norm = (pn[0] + pn[2]) + (pn[1] + pn[3]);
+  float ipnorm_inv = 1.0f / ip_norm;
+  if (isnan(ipnorm_inv)) ipnorm_inv = 1.0f;
+  float a[4] = {0, 0, 0, 0}, b[4] = {0, 0, 0, 0}, cc[4] = {0, 0, 0, 0};
+  memset(node, 0, code_bytes);
+  for (uint32_t j = 0; j < dim; j++) {
+    float r = x[j] - c[j];
+    int bit = r >= 0.0f;
+    if (bit) node[j / 8] |= (uint8_t)(1u << (j % 8));
+    float xu = (float)bit + (-0.5f);
+    a[j % 4] = fmaf(r, xu, a[j % 4]);
+    b[j % 4] = fmaf(c[j], xu, b[j % 4]);
+    cc[j % 4] = fmaf(r, c[j], cc[j % 4]);
+  }
+  float ip_resi_xucb = (a[0] + a[2]) + (a[1] + a[3]);
+  const float ip_cent_xucb = (b[0] + b[2]) + (b[1] + b[3]);
+  const float ip_resi_cent = (cc[0] + cc[2]) + (cc[1] + cc[3]);
+  if (ip_resi_xucb == 0.0f) ip_resi_xucb = INFINITY;
+  float f_add, f_rescale;
+  if (!ip) {
+    f_add = l2_sqr + ((2.0f * l2_sqr) * ip_cent_xucb) / ip_resi_xucb;
+    f_rescale = (ipnorm_inv * -2.0f) * l2_norm;
+  } else {
+    f_add = (1.0f - ip_resi_cent) + (l2_sqr * ip_cent_xucb) / ip_resi_xucb;
+    f_rescale = ipnorm_inv * -l2_norm;
+  }
+  memcpy(node + code_bytes, &f_add, 4);
+  memcpy(node + code_bytes + 4, &f_rescale, 4);
+}
+
+uint32_t orc_rabitq_code_bytes(uint32_t dim) { return ((dim + 7) / 8 + 3) / 4 * 4; }
+
+typedef struct { const float *rows; uint64_t stride; const float *c; uint32_t dim; int ip; uint8_t *out; } rq_ctx;
+
+static void rq_body(void *vctx, long i) {
+  rq_ctx *c = (rq_ctx *)vctx;
+  const uint32_t cb = orc_rabitq_code_bytes(c->dim);
+  rabitq_row(c->rows + (size_t)i * c->stride, c->c, c->dim, c->ip, c->out + (size_t)i * (cb + 8), cb);
+}
+
+void orc_rabitq_quantize(const float *rows, uint64_t n, uint64_t stride, uint32_t dim,
+                         const float *centroid, int ip, uint8_t *out) {
+  rq_ctx c = {rows, stride, centroid, dim, ip, out};
+  parallel_for((long)n, rq_body, &c);
+}
+
+/* Column means of n fp16 rows (dpad stride) accumulated in double in row
+ * order, rounded to float: the centroid the graph's RaBitQ codes use. */
+void orc_rabitq_centroid(const uint16_t *vec, uint64_t n, uint32_t dim, uint32_t dpad, float *out) {
+  for (uint32_t j = 0; j < dim; j++) {
+    double s = 0.0;
+    for (uint64_t i = 0; i < n; i++) s += (double)orc_half_to_float(vec[i * dpad + j]);
+    out[j] = (float)(s / (double)n);
+  }
+}
+
 /* graph_beam_search_kernel (graph_beam_search.cuh:55-270) with the LSH
  * (directional_beam_search.cuh:31-192) or PQ (pq_beam_search.cuh:31-201)
  * estimator, for one query.  Unfilled outputs are (0x7FFFFFFF, FLT_MAX). */
@@ -717,7 +863,15 @@ void orc_dir_search_one(const orc_graph *g, const orc_dir *dd, const uint16_t *q
   float q_sq = 0.f, inv_nd = 0.f;
   uint32_t fc = 0, count = 1;
   buf[0].idx = g->medoid; buf[0].dist = 0.0f; buf[0].visited = 0;
-  if (dd->kind == 0) {
+  /* RaBitQ query state: 4-bit query planes, offsets, centroid term */
+  uint32_t *rq_planes = NULL;
+  float rq_vl = 0.f, rq_delta = 0.f, rq_gadd = 0.f;
+  int rq_S = 0;
+  if (dd->kind == 2) {
+    const uint32_t dim = g->dim, nw = (dim + 31) / 32;
+    rq_planes = (uint32_t *)calloc((size_t)4 * nw, sizeof(uint32_t));
+    rabitq_query_prep(q, dim, dd->rq_centroid, ip, rq_planes, &rq_vl, &rq_delta, &rq_S, &rq_gadd);
+  } else if (dd->kind == 0) {
     inv_nd = 1.0f / dd->norm_denom;
   } else {
     const uint32_t M = dd->pq_m, dsub = dd->pq_dsub;
@@ -753,7 +907,7 @@ void orc_dir_search_one(const orc_graph *g, const orc_dir *dd, const uint16_t *q
     buf[f].visited = 1;
     const uint32_t u = buf[f].idx;
     float exact_u, dist_u;
-    if (dd->kind == 0) {
+    if (dd->kind == 0 || dd->kind == 2) {
       exact_u = dir_visit_exact(g, q, u, ip, ip ? NULL : qu);
       dist_u = ip ? -exact_u : exact_u;
     } else {
@@ -778,7 +932,11 @@ void orc_dir_search_one(const orc_graph *g, const orc_dir *dd, const uint16_t *q
       orc_entry *en = &buf[off + e];
       if (en->idx == ORC_EMPTY_IDX) continue;
       float est;
-      if (dd->kind == 0) {
+      if (dd->kind == 2) {
+        est = rabitq_estimate(dd->rq_store + (size_t)(en->idx - g->global_offset) * dd->rq_node_bytes,
+                              dd->rq_code_bytes, g->dim, rq_planes, rq_vl, rq_delta, rq_S,
+                              rq_gadd, ip);
+      } else if (dd->kind == 0) {
         float dot = 0.f;
         for (uint32_t r = 0; r < dd->k_ranks; r++) {
           uint32_t word, coord, neg;
@@ -828,7 +986,7 @@ void orc_dir_search_one(const orc_graph *g, const orc_dir *dd, const uint16_t *q
     out_idx[out] = idx; out_dist[out] = fr[i].dist; out++;
   }
   for (; out < k; out++) { out_idx[out] = ORC_EMPTY_IDX; out_dist[out] = 3.402823466e+38f; }
-  free(buf); free(tmp); free(fr); free(qu); free(lut);
+  free(buf); free(tmp); free(fr); free(qu); free(lut); free(rq_planes);
 }
 
 typedef struct {

@@ -183,6 +183,8 @@ class _Dir(C.Structure):
         ("packed", C.c_void_p), ("mag_sq", C.c_void_p), ("c", C.c_void_p),
         ("norm_denom", C.c_float), ("pq_m", C.c_uint32), ("pq_dsub", C.c_uint32),
         ("centroids", C.c_void_p), ("codes", C.c_void_p), ("norms", C.c_void_p),
+        ("rq_store", C.c_void_p), ("rq_node_bytes", C.c_uint32), ("rq_code_bytes", C.c_uint32),
+        ("rq_centroid", C.c_void_p),
     ]
 
 
@@ -194,7 +196,8 @@ def set_dir_mode(m: int) -> None:
 
 def dir_search(g: OracleGraph, kind: str, art: dict, queries: np.ndarray, k: int,
                beam_width: int, limit: int):
-    """directional_search ('lsh') or pq_search ('pq') given the artifacts."""
+    """directional_search ('lsh'), pq_search ('pq') or the RaBitQ-estimated
+    search ('rabitq') given the artifacts."""
     L = lib()
     L.orc_dir_search.argtypes = [C.POINTER(_Graph), C.POINTER(_Dir), C.c_void_p, C.c_uint32,
                                  C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
@@ -205,7 +208,15 @@ def dir_search(g: OracleGraph, kind: str, art: dict, queries: np.ndarray, k: int
         keep[name] = a
         return _p(a)
     d = _Dir()
-    if kind == "lsh":
+    if kind == "rabitq":
+        store = np.ascontiguousarray(art["rq_store"], np.uint8)
+        keep["store"] = store
+        d.kind = 2
+        d.rq_store = _p(store)
+        d.rq_node_bytes = store.shape[1]
+        d.rq_code_bytes = store.shape[1] - 8
+        d.rq_centroid = arr("rq_centroid", np.float32)
+    elif kind == "lsh":
         packed = np.ascontiguousarray(art["lsh_packed"])
         keep["packed"] = packed
         d.kind, d.k_ranks, d.packed_bytes = 0, int(art["k_ranks"]), packed.dtype.itemsize
@@ -262,4 +273,34 @@ def row_norms_exact(g: OracleGraph):
     out = np.zeros(g.n, np.float32)
     gs = g._struct()
     L.orc_row_norms(C.byref(gs), _p(out))
+    return out
+
+
+# ── RaBitQ (1 bit per dimension) ─────────────────────────────────────────
+def rabitq_code_bytes(dim: int) -> int:
+    return ((dim + 7) // 8 + 3) // 4 * 4
+
+
+def rabitq_quantize(rows: np.ndarray, centroid: np.ndarray, ip: bool) -> np.ndarray:
+    """rabitq_quantize_kernel<1> restated: rows [n, dim] float32 (already
+    rotated) -> node store [n, code_bytes + 8] uint8."""
+    L = lib()
+    L.orc_rabitq_quantize.argtypes = [C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint32, C.c_void_p,
+                                      C.c_int, C.c_void_p]
+    L.orc_rabitq_quantize.restype = None
+    x = np.ascontiguousarray(rows, np.float32)
+    n, dim = x.shape
+    c = np.ascontiguousarray(centroid, np.float32)
+    out = np.zeros((n, rabitq_code_bytes(dim) + 8), np.uint8)
+    L.orc_rabitq_quantize(_p(x), n, dim, dim, _p(c), int(bool(ip)), _p(out))
+    return out
+
+
+def rabitq_centroid(g: "OracleGraph") -> np.ndarray:
+    """Column means of the graph rows, double accumulation in row order."""
+    L = lib()
+    L.orc_rabitq_centroid.argtypes = [C.c_void_p, C.c_uint64, C.c_uint32, C.c_uint32, C.c_void_p]
+    L.orc_rabitq_centroid.restype = None
+    out = np.zeros(g.dim, np.float32)
+    L.orc_rabitq_centroid(_p(g.vec), g.n, g.dim, g.dpad, _p(out))
     return out

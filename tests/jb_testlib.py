@@ -150,3 +150,28 @@ def oracle_from_handle(h: int, n: int, dim: int, R: int, metric: int) -> "O.Orac
     e, d, c = get_edges(h, n, R)
     g.edges[:], g.edist[:], g.counts[:] = e, d, c
     return g
+
+
+def dir_search_kind(h: int, kind: int, Q: np.ndarray, k: int, bw: int, limit: int | None = None):
+    """jb_graph_directional_search with an explicit kind (0 LSH, 1 PQ, 2 RaBitQ)."""
+    import torch
+    q = torch.from_numpy(O.pad_rows(Q)).cuda()
+    nq = q.shape[0]
+    oi = torch.empty(nq, k, dtype=torch.int32, device="cuda")
+    od = torch.empty(nq, k, dtype=torch.float32, device="cuda")
+    limit = 2 * bw if limit is None else limit
+    _lib.call("jb_graph_directional_search", h, kind, q.data_ptr(), nq, q.shape[1], oi.data_ptr(),
+              od.data_ptr(), k, bw, limit, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return oi.cpu().numpy(), od.cpu().numpy()
+
+
+def rotate_on_device(Q: np.ndarray, dim: int, seed: int) -> np.ndarray:
+    """Rows rotated by the same tensor-core GEMM the search uses, as fp16 [n, dim]."""
+    import torch
+    x = torch.from_numpy(O.pad_rows(Q)).cuda()
+    y = torch.empty_like(x)
+    _lib.call("jb_rotate_rows", dim, seed, x.data_ptr(), y.data_ptr(), x.shape[0], 1,
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return y.cpu().numpy().view(np.float16)[:, :dim]
