@@ -599,6 +599,126 @@ def run_rotation(args):
         print(json.dumps(line), flush=True)
 
 
+# ── config 3 (directional) and config 4 (RaBitQ) ─────────────────────────
+def _timed_qps(fn, nq, steps, warmup):
+    """Device time of fn() (CUDA events, median over steps) -> (QPS, ms)."""
+    for _ in range(warmup):
+        fn()
+    ts = []
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    ms = float(np.median(ts))
+    return nq / (ms / 1e3), ms
+
+
+def run_directional(args):
+    """Config 3: config-1 rows (100k x 128 N(0,1), seed 0; 1k queries, seed
+    1), R = 32, prerotation seed 4; LSH with k_ranks 4 and 16 (32,768
+    calibration samples) and PQ with M = k_ranks and M = 32 (4-dim
+    subspaces, k-means 20 iterations, seed 5); directional_search /
+    pq_search at beam 64 and 128.  One JSON line per estimator."""
+    import jasper_b200 as jasper
+    from jasper_b200 import _lib, synthetic
+    torch.cuda.set_device(0)
+    X = torch.from_numpy(synthetic.gaussian(100_000, 128, 0)).cuda()
+    Q = torch.from_numpy(synthetic.gaussian(1000, 128, 1)).cuda()
+    gt = exact_gt(X, Q, K)
+    for kr in (4, 16):
+        g = jasper.Graph.build(X, n_neighbors=32, alpha=1.2, build_lsh=True, build_pq=True,
+                               k_ranks=kr, prerotate_seed=4, lsh_samples=32768,
+                               pq_kmeans_iter=20, pq_seed=5)
+        runs = [("lsh", kr, g.directional_search), ("pq", kr, g.pq_search)]
+        for name, m, fn in runs:
+            line = {"mode": "directional", "config": "config3", "estimator": name,
+                    "k_ranks" if name == "lsh" else "pq_m": m}
+            for bw in (64, 128):
+                ids, _ = fn(Q, k=K, beam_width=bw)
+                qps, ms = _timed_qps(lambda: fn(Q, k=K, beam_width=bw), 1000, args.steps, args.warmup)
+                line[f"bw{bw}"] = {"recall_at_10": round(recall_at_k(ids, gt), 4),
+                                   "qps": round(qps, 1), "ms": round(ms, 4)}
+            print(json.dumps(line), flush=True)
+        if kr == 4:
+            # the 32 x 4-dim codebooks BASELINE asks for (the reference only has M = k_ranks)
+            _lib.call("jb_graph_build_pq", g._handle, 32, 40000, 20, 5)
+            line = {"mode": "directional", "config": "config3", "estimator": "pq", "pq_m": 32}
+            for bw in (64, 128):
+                ids, _ = g.pq_search(Q, k=K, beam_width=bw)
+                qps, ms = _timed_qps(lambda: g.pq_search(Q, k=K, beam_width=bw), 1000, args.steps,
+                                     args.warmup)
+                line[f"bw{bw}"] = {"recall_at_10": round(recall_at_k(ids, gt), 4),
+                                   "qps": round(qps, 1), "ms": round(ms, 4)}
+            print(json.dumps(line), flush=True)
+        g.free()
+
+
+def gen_relu_sphere_gpu(n, dim, n_centers, sigma, seed, center_seed, dev):
+    """Config-4 rows on the GPU: Gaussian mixture (centres N(0,1)), per-dim
+    sigma, ReLU, L2-normalised, fp16."""
+    gc = torch.Generator(device=dev).manual_seed(center_seed)
+    centers = torch.randn(n_centers, dim, generator=gc, device=dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    out = torch.empty(n, dim, dtype=torch.float16, device=dev)
+    for i in range(0, n, 1 << 18):
+        m = min(1 << 18, n - i)
+        c = torch.randint(0, n_centers, (m,), generator=g, device=dev)
+        x = (centers[c] + sigma * torch.randn(m, dim, generator=g, device=dev)).clamp_(min=0)
+        x = x / x.norm(dim=1, keepdim=True).clamp_(min=1e-12)
+        out[i:i + m] = x.half()
+    return out
+
+
+def run_rabitq(args):
+    """Config 4: 1M x 960 ReLU-clamped, L2-normalised Gaussian-mixture rows
+    (256 centres, sigma 0.3, seed 6), 1k queries (seed 7), inner product,
+    R = 64, alpha = 1.0; RaBitQ 1-bit codes; k = 10, beam 64 / 128 / 256:
+    the exact beam search with the RaBitQ candidate filter (margin 1) and
+    without it (exact), with rows read per query."""
+    import jasper_b200 as jasper
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    n = args.n
+    X = gen_relu_sphere_gpu(n, 960, 256, 0.3, 6, 6, dev)
+    Q = gen_relu_sphere_gpu(1000, 960, 256, 0.3, 7, 6, dev)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    sims = []
+    for q0 in range(0, 1000, 250):
+        s = Q[q0:q0 + 250].float() @ X.float().T
+        sims.append(s.topk(K, dim=1).indices.int())
+    gt = torch.cat(sims)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    g = jasper.Graph.build(X, n_neighbors=64, distance="ip", alpha=1.0, build_rabitq=True)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    line = {"mode": "rabitq", "config": "config4", "rows": n, "dim": 960,
+            "build": {"seconds": round(build_s, 3), "mvec_per_s": round(n / build_s / 1e6, 4),
+                      "note": "graph construction + prerotation + RaBitQ codes"}}
+    from jasper_b200 import _lib
+    for bw in (64, 128, 256):
+        # margin 1e30: the filter never drops anything (the exact search)
+        for name, margin in (("rabitq", 1.0), ("exact", 1e30)):
+            ids, _ = g.rabitq_search(Q, k=K, beam_width=bw, margin=margin)
+            qps, ms = _timed_qps(lambda: g.rabitq_search(Q, k=K, beam_width=bw, margin=margin),
+                                 1000, args.steps, args.warmup)
+            st = torch.zeros(1000, 5, dtype=torch.int32, device=dev)
+            oi = torch.empty(1000, K, dtype=torch.int32, device=dev)
+            od = torch.empty(1000, K, dtype=torch.float32, device=dev)
+            _lib.call("jb_graph_search_rabitq", g._handle, Q.data_ptr(), 1000, 960, oi.data_ptr(),
+                      od.data_ptr(), K, bw, 2 * bw, float(margin), st.data_ptr(),
+                      torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            line[f"{name}_bw{bw}"] = {"recall_at_10": round(recall_at_k(ids, gt), 4),
+                                      "qps": round(qps, 1), "ms": round(ms, 4),
+                                      "rows_read_per_query": round(st[:, 2].float().mean().item(), 1)}
+    print(json.dumps(line), flush=True)
+    g.free()
+
+
 # ── reference arm ─────────────────────────────────────────────────────────
 def run_reference(args):
     ws, rank, local = dist_env()
@@ -687,9 +807,11 @@ def main():
     ap.add_argument("--nq", type=int, default=10_000)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", default="replicas", choices=["replicas", "sharded", "rotation"],
+    ap.add_argument("--mode", default="replicas",
+                    choices=["replicas", "sharded", "rotation", "directional", "rabitq"],
                     help="replicas: config 2 per GPU (default); sharded: config 5 range "
-                         "shards; rotation: the prerotation GEMM alone")
+                         "shards; rotation: the prerotation GEMM alone; directional: "
+                         "config 3 (LSH / PQ); rabitq: config 4")
     ap.add_argument("--n-shard", type=int, default=12_500_000,
                     help="rows per GPU in --mode sharded (config 5: 12.5M)")
     args = ap.parse_args()
@@ -701,6 +823,10 @@ def main():
         run_sharded(args)
     elif args.mode == "rotation":
         run_rotation(args)
+    elif args.mode == "directional":
+        run_directional(args)
+    elif args.mode == "rabitq":
+        run_rabitq(args)
     else:
         run_jasper(args)
 

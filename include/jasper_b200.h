@@ -274,11 +274,26 @@ int jb_rabitq_quantize(const float* rows, uint64_t n, uint32_t dim, const float*
                        const float* centroid, int32_t metric, uint8_t* out, void* stream);
 
 /* RaBitQ codes of the graph's own rows (prerotated when the graph was built
- * with prerotation) around their column mean; enables
- * jb_graph_directional_search(kind = JB_DIR_RABITQ).  No reference
- * counterpart: the reference quantizes but has no RaBitQ search.
- * Synchronous. */
+ * with prerotation) around their column mean, plus each row's estimate error
+ * scale; enables jb_graph_search_rabitq.  No reference counterpart: the
+ * reference quantizes but has no RaBitQ search.  Synchronous. */
 int jb_graph_build_rabitq(int64_t handle);
+
+/* The beam search with exact distances (as jb_graph_search; queries are
+ * prerotated when the graph is) plus a RaBitQ candidate filter: while the
+ * beam is full, a new neighbour whose estimate minus margin * |q - c| *
+ * err(v) exceeds the beam's worst exact distance is skipped without reading
+ * its row.  margin = 1 keeps the exact search's recall in our tests; larger
+ * is more conservative.  Device pointers; unfilled slots (-1, 1e30); stats as
+ * jb_graph_search_stats (NULL for none).  jb_graph_directional_search with
+ * kind JB_DIR_RABITQ runs this with margin 1.  Asynchronous. */
+int jb_graph_search_rabitq(int64_t handle, const uint16_t* queries, uint64_t n_queries,
+                           uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
+                           uint32_t beam_width, uint32_t limit, float margin, uint32_t* stats,
+                           void* stream);
+
+/* Each row's estimate error scale [n] f32 (host or device). */
+int jb_graph_get_rabitq_err(int64_t handle, float* err);
 
 /* Attach / read RaBitQ payloads (host arrays): store [n][node_bytes] as
  * jb_rabitq_quantize writes it, centroid [dim] f32.  Either output pointer

@@ -346,15 +346,35 @@ class Graph:
         return self._dir_search(1, "pq_search", queries, k, beam_width, limit, print_throughput)
 
     def rabitq_search(self, queries: torch.Tensor, k: int = 10, beam_width: int = 128,
-                      limit: int | None = None, print_throughput: bool = False):
-        """Beam search scored by the RaBitQ 1-bit estimator (codes built with
-        ``build_rabitq=True``): candidates are ranked by the estimate, every
-        expanded node by its exact distance (the directional search loop).
+                      limit: int | None = None, margin: float = 1.0,
+                      print_throughput: bool = False):
+        """Beam search with exact distances where RaBitQ 1-bit estimates
+        (codes built with ``build_rabitq=True``) skip neighbours that cannot
+        enter the full beam: a neighbour is read only if its estimate minus
+        ``margin`` error scales is below the beam's worst distance.  An
+        addition of this package (the reference has no RaBitQ search).
         Returns (int32 [nq, k] ids, float32 [nq, k] exact distances)."""
         self._check_alive()
         if not self._is_directional or not self._has_rabitq:
             raise RuntimeError("rabitq_search() requires a graph built with build_rabitq=True")
-        return self._dir_search(2, "rabitq_search", queries, k, beam_width, limit, print_throughput)
+        queries = self._check_queries(queries)
+        nq = queries.size(0)
+        out_i = torch.empty(nq, k, dtype=torch.int32, device=queries.device)
+        out_d = torch.empty(nq, k, dtype=torch.float32, device=queries.device)
+        limit = beam_width * 2 if limit is None else limit
+        if print_throughput:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+        _lib.call("jb_graph_search_rabitq", self._handle, _ptr(queries), nq, self._dim,
+                  _ptr(out_i), _ptr(out_d), k, beam_width, limit, float(margin), None,
+                  _stream_ptr(queries.device))
+        if print_throughput:
+            e1.record()
+            e1.synchronize()
+            ms = e0.elapsed_time(e1)
+            print(f"[rabitq_search] duration={ms}ms, throughput={nq * 1000.0 / max(ms, 1e-9)}")
+        return out_i, out_d
 
     # ── rows, ids, deletion ───────────────────────────────────────────
     def get_vector(self, stable_id: int) -> torch.Tensor:

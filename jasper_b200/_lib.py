@@ -77,6 +77,8 @@ SIGNATURES: dict[str, list] = {
     "jb_graph_build_rabitq": [_I64],
     "jb_graph_set_rabitq": [_I64, _U32, _P, _P],
     "jb_graph_get_rabitq": [_I64, C.POINTER(_U32), _P, _P],
+    "jb_graph_search_rabitq": [_I64, _P, _U64, _U32, _P, _P, _U32, _U32, _U32, C.c_float, _P, _P],
+    "jb_graph_get_rabitq_err": [_I64, _P],
 }
 
 

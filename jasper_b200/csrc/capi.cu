@@ -109,9 +109,12 @@ void check_metric(int32_t metric) {
 
 // Device search over queries with any row stride: rows whose stride is not
 // the padded dim are first packed into a padded scratch copy.
+// rq_margin >= 0 turns on the RaBitQ candidate filter; `rotate` applies the
+// graph's prerotation to the queries first.
 void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint32_t row_stride,
                  int32_t* out_idx, float* out_dist, uint32_t k, uint32_t bw, uint32_t limit,
-                 uint32_t* stats, uint32_t* seen, cudaStream_t st) {
+                 uint32_t* stats, uint32_t* seen, cudaStream_t st, float rq_margin = -1.0f,
+                 bool rotate = false) {
   if (nq == 0) return;
   if (nq > 0x7FFFFFFFull) throw std::invalid_argument("too many queries");
   if (k == 0) throw std::invalid_argument("k must be > 0");
@@ -122,12 +125,20 @@ void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint3
   void* packed = nullptr;
   void* counter = nullptr;
   const bool aligned = (reinterpret_cast<uintptr_t>(queries) % 16) == 0;
-  if (row_stride != g.dpad || !aligned) {
+  if (row_stride != g.dpad || !aligned || rotate) {
     cuda_check(cudaMallocAsync(&packed, size_t(nq) * g.dpad * 2, st), "alloc packed queries");
     cuda_check(cudaMemsetAsync(packed, 0, size_t(nq) * g.dpad * 2, st), "clear packed queries");
     cuda_check(cudaMemcpy2DAsync(packed, size_t(g.dpad) * 2, queries, size_t(row_stride) * 2,
                                  size_t(g.dim) * 2, nq, cudaMemcpyDefault, st),
                "pack queries");
+    if (rotate) {
+      try {
+        jb::rotate_rows_inplace(g, static_cast<uint16_t*>(packed), nq, st);
+      } catch (...) {
+        cudaFreeAsync(packed, st);
+        throw;
+      }
+    }
     q = static_cast<const uint16_t*>(packed);
   }
   cuda_check(cudaMallocAsync(&counter, jb::kSearchScratchBytes, st), "alloc search scratch");
@@ -145,6 +156,19 @@ void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint3
   a.work_counter = static_cast<uint32_t*>(counter);
   a.stats = stats;
   a.seen_bits = seen;
+  if (rq_margin >= 0.0f) {
+    if (!g.dir.has_rabitq) throw std::runtime_error("graph has no RaBitQ codes built");
+    if (!g.dir.rq_err)
+      throw std::runtime_error("graph has RaBitQ codes but no error scales (build them with "
+                               "jb_graph_build_rabitq)");
+    a.rq_on = 1;
+    a.rq_store = g.dir.rq_store;
+    a.rq_node_bytes = g.dir.rq_node_bytes;
+    a.rq_code_bytes = g.dir.rq_code_bytes;
+    a.rq_centroid = g.dir.rq_centroid;
+    a.rq_err = g.dir.rq_err;
+    a.rq_margin = rq_margin;
+  }
   try {
     jb::launch_search(a, st);
   } catch (...) {
@@ -514,6 +538,11 @@ int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* qu
       throw std::runtime_error("Graph " + std::to_string(handle) + " has no PQ artifacts built");
     if (kind == JB_DIR_RABITQ && !d.has_rabitq)
       throw std::runtime_error("Graph " + std::to_string(handle) + " has no RaBitQ codes built");
+    if (kind == JB_DIR_RABITQ) {  // the exact search with the RaBitQ filter, margin 1
+      search_impl(*g, queries, n_queries, row_stride, out_idx, out_dist, k, beam_width, limit,
+                  nullptr, nullptr, static_cast<cudaStream_t>(stream), 1.0f, d.prerotate);
+      return;
+    }
     if (n_queries == 0) return;
     if (!queries || !out_idx || !out_dist) throw std::invalid_argument("null pointer argument");
     if (row_stride < g->dim) throw std::invalid_argument("row_stride < dim");
@@ -548,10 +577,6 @@ int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* qu
     a.centroids = d.pq_centroids;
     a.codes = d.pq_codes;
     a.norms = d.norms;
-    a.rq_store = d.rq_store;
-    a.rq_node_bytes = d.rq_node_bytes;
-    a.rq_code_bytes = d.rq_code_bytes;
-    a.rq_centroid = d.rq_centroid;
     a.queries = q;
     a.nq = uint32_t(n_queries);
     a.k = k;
@@ -797,6 +822,29 @@ int jb_graph_get_rabitq(int64_t handle, uint32_t* out_node_bytes, uint8_t* store
     if (out_node_bytes) *out_node_bytes = d.rq_node_bytes;
     if (store) cuda_check(cudaMemcpy(store, d.rq_store, size_t(g->n) * d.rq_node_bytes, cudaMemcpyDefault), "codes");
     if (centroid) cuda_check(cudaMemcpy(centroid, d.rq_centroid, size_t(g->dim) * 4, cudaMemcpyDefault), "centroid");
+  });
+}
+
+int jb_graph_search_rabitq(int64_t handle, const uint16_t* queries, uint64_t n_queries,
+                           uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
+                           uint32_t beam_width, uint32_t limit, float margin, uint32_t* stats,
+                           void* stream) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (!(margin >= 0.0f)) throw std::invalid_argument("margin must be >= 0");
+    search_impl(*g, queries, n_queries, row_stride, out_idx, out_dist, k, beam_width, limit, stats,
+                nullptr, static_cast<cudaStream_t>(stream), margin, g->dir.prerotate);
+  });
+}
+
+int jb_graph_get_rabitq_err(int64_t handle, float* err) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (!g->dir.has_rabitq || !g->dir.rq_err) throw std::runtime_error("graph has no RaBitQ codes built");
+    if (!err) throw std::invalid_argument("err is null");
+    cuda_check(cudaMemcpy(err, g->dir.rq_err, size_t(g->n) * 4, cudaMemcpyDefault), "rabitq errors");
   });
 }
 

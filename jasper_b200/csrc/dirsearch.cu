@@ -1,5 +1,5 @@
-// dirsearch.cu -- directional beam search (cross-polytope LSH, PQ-ADC or
-// RaBitQ estimated neighbour distances) for sm_100a, one warp per query.
+// dirsearch.cu -- directional beam search (cross-polytope LSH or PQ-ADC
+// estimated neighbour distances) for sm_100a, one warp per query.
 //
 // Reproduces graph_beam_search_kernel (include/jasper/beam_search/
 // graph_beam_search.cuh:55-270) with the lsh_estimator
@@ -21,12 +21,7 @@
 //    xor-butterfly reduction is replayed in the same order;
 //  * the PQ lookup table is built one centroid per lane: each lane forms the
 //    32 lane-strided partial dot products of the reference's warp-per-centroid
-//    build and adds them in that warp's butterfly order;
-//  * the RaBitQ estimator (no reference search uses RaBitQ codes; this one
-//    is ours) scores a neighbour from its node's 1-bit code and two factors:
-//    the query is quantised to 4 bit-planes once, <code, q> is a sum of
-//    popcounts of code & plane words, then
-//    est = f_add + f_rescale * <code - 1/2, q~> + (|q - c|^2 or -<c, q> - 1).
+//    build and adds them in that warp's butterfly order.
 #include <cfloat>
 #include <stdexcept>
 #include <string>
@@ -41,7 +36,7 @@ constexpr uint32_t kEmpty31 = 0x7FFFFFFFu;
 __host__ __device__ inline size_t a16(size_t x) { return (x + 15) & ~size_t(15); }
 
 struct DirLayout {
-  size_t beam, cand, qh, qu, lut, rq, fid, fdist, total;
+  size_t beam, cand, qh, qu, lut, fid, fdist, total;
 };
 
 __host__ __device__ inline DirLayout dir_layout(uint32_t bwcap, uint32_t dpad, int kind,
@@ -54,7 +49,6 @@ __host__ __device__ inline DirLayout dir_layout(uint32_t bwcap, uint32_t dpad, i
   L.qh = o; o += a16(size_t(dpad) * 2);
   L.qu = o; o += a16(size_t(dpad) * 2);
   L.lut = o; o += kind == kDirPq ? a16(size_t(pq_m) * 256 * 4) : 0;
-  L.rq = o; o += kind == kDirRabitq ? a16(size_t(4) * ((dpad + 31) / 32) * 4) : 0;
   L.fid = o; o += a16(size_t(k) * 4);
   L.fdist = o; o += a16(size_t(k) * 4);
   L.total = o;
@@ -132,8 +126,6 @@ __global__ void __launch_bounds__(128) dir_search_kernel(DirSearchArgs a) {
   uint16_t* qh = reinterpret_cast<uint16_t*>(base + L.qh);
   uint16_t* qu = reinterpret_cast<uint16_t*>(base + L.qu);
   float* lut = reinterpret_cast<float*>(base + L.lut);
-  uint32_t* planes = reinterpret_cast<uint32_t*>(base + L.rq);
-  const uint32_t dim = g.dim, nw = (dim + 31) / 32;
   uint32_t* fid = reinterpret_cast<uint32_t*>(base + L.fid);
   float* fdist = reinterpret_cast<float*>(base + L.fdist);
   const uint32_t lo = g.global_offset;
@@ -152,60 +144,6 @@ __global__ void __launch_bounds__(128) dir_search_kernel(DirSearchArgs a) {
     __syncwarp();
 
     float q_sq = 0.0f;
-    // RaBitQ query state (no reference counterpart): 4-bit planes of the
-    // query, offsets vl / delta, S = sum of the 4-bit values, centroid term.
-    float rq_vl = 0.0f, rq_delta = 0.0f, rq_gadd = 0.0f;
-    int rq_S = 0;
-    if constexpr (KIND == kDirRabitq) {
-      const __half* qv = reinterpret_cast<const __half*>(qh);
-      float vl = __int_as_float(0x7F800000), vr = -vl;
-      for (uint32_t i = lane; i < dim; i += 32) {
-        const float x = __half2float(qv[i]);
-        vl = fminf(vl, x);
-        vr = fmaxf(vr, x);
-      }
-#pragma unroll
-      for (int d = 16; d > 0; d >>= 1) {
-        vl = fminf(vl, __shfl_xor_sync(kFull, vl, d));
-        vr = fmaxf(vr, __shfl_xor_sync(kFull, vr, d));
-      }
-      const float range = __fsub_rn(vr, vl);
-      const float inv = range > 0.0f ? __fdiv_rn(15.0f, range) : 0.0f;
-      int S = 0;
-      for (uint32_t w = 0; w < nw; w++) {
-        const uint32_t i = 32 * w + lane;
-        int qq = 0;
-        if (i < dim) {
-          qq = __float2int_rn(__fmul_rn(__fsub_rn(__half2float(qv[i]), vl), inv));
-          qq = qq < 0 ? 0 : (qq > 15 ? 15 : qq);
-        }
-        S += qq;
-#pragma unroll
-        for (int p = 0; p < 4; p++) {
-          const uint32_t bits = __ballot_sync(kFull, (qq >> p) & 1);
-          if (lane == 0) planes[p * nw + w] = bits;
-        }
-      }
-#pragma unroll
-      for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(kFull, S, d);
-      float acc = 0.0f;
-      for (uint32_t i = lane; i < dim; i += 32) {
-        const float x = __half2float(qv[i]);
-        const float ci = __ldg(a.rq_centroid + i);
-        if constexpr (IP) {
-          acc = __fmaf_rn(ci, x, acc);
-        } else {
-          const float dd = __fsub_rn(x, ci);
-          acc = __fmaf_rn(dd, dd, acc);
-        }
-      }
-      acc = butterfly32(acc);
-      rq_vl = vl;
-      rq_delta = __fdiv_rn(range, 15.0f);
-      rq_S = S;
-      rq_gadd = IP ? -acc : acc;
-      __syncwarp();
-    }
     if constexpr (KIND == kDirPq) {
       // pq_build_lut (pq_beam_search.cuh:31-60), one centroid per lane.
       const uint32_t dsub = a.pq_dsub;
@@ -273,9 +211,6 @@ __global__ void __launch_bounds__(128) dir_search_kernel(DirSearchArgs a) {
       if constexpr (KIND == kDirLsh) {
         exact_u = visit_exact<IP>(qh, urow, IP ? nullptr : qu, nv4, lane);
         dist_u = IP ? -exact_u : exact_u;
-      } else if constexpr (KIND == kDirRabitq) {
-        exact_u = visit_exact<IP>(qh, urow, nullptr, nv4, lane);
-        dist_u = IP ? -exact_u : exact_u;
       } else {
         exact_u = visit_exact<true>(qh, urow, nullptr, nv4, lane);  // <q, u>
         dist_u = IP ? -exact_u : q_sq - 2.0f * exact_u + a.norms[u - lo];
@@ -312,25 +247,7 @@ __global__ void __launch_bounds__(128) dir_search_kernel(DirSearchArgs a) {
           ok = v - lo < g.n;
         }
         if (ok) {
-          if constexpr (KIND == kDirRabitq) {
-            // est = f_add + f_rescale * <code - 1/2, q~> + gadd, with
-            // <code - 1/2, q~> = 0.5 vl (2 popc(b) - dim) + 0.5 delta (2 A - S)
-            const uint8_t* node = a.rq_store + size_t(v - lo) * a.rq_node_bytes;
-            const uint32_t* cw = reinterpret_cast<const uint32_t*>(node);
-            int A = 0, pb = 0;
-            for (uint32_t w = 0; w < nw; w++) {
-              const uint32_t b = __ldg(cw + w);
-              pb += __popc(b);
-              A += __popc(b & planes[w]) + (__popc(b & planes[nw + w]) << 1) +
-                   (__popc(b & planes[2 * nw + w]) << 2) + (__popc(b & planes[3 * nw + w]) << 3);
-            }
-            const float f_add = __ldg(reinterpret_cast<const float*>(node + a.rq_code_bytes));
-            const float f_rescale = __ldg(reinterpret_cast<const float*>(node + a.rq_code_bytes) + 1);
-            const float t1 = __fmul_rn(float(2 * pb - int(dim)), __fmul_rn(0.5f, rq_vl));
-            const float ipx = __fmaf_rn(float(2 * A - rq_S), __fmul_rn(0.5f, rq_delta), t1);
-            est = __fadd_rn(__fmaf_rn(f_rescale, ipx, f_add), rq_gadd);
-            if constexpr (IP) est = __fsub_rn(est, 1.0f);
-          } else if constexpr (KIND == kDirLsh) {
+          if constexpr (KIND == kDirLsh) {
             const __half* ev = reinterpret_cast<const __half*>(IP ? qh : qu);
             float dot_acc = 0.0f;
             const size_t wbase = (size_t(lu) * R + e) * a.k_ranks;
@@ -467,8 +384,6 @@ template <uint32_t BWCAP>
 void dispatch_kind(const DirSearchArgs& a, cudaStream_t st) {
   const bool ip = a.g.metric == kIP;
   if (a.kind == kDirLsh) return ip ? launch_t<BWCAP, kDirLsh, true>(a, st) : launch_t<BWCAP, kDirLsh, false>(a, st);
-  if (a.kind == kDirRabitq)
-    return ip ? launch_t<BWCAP, kDirRabitq, true>(a, st) : launch_t<BWCAP, kDirRabitq, false>(a, st);
   return ip ? launch_t<BWCAP, kDirPq, true>(a, st) : launch_t<BWCAP, kDirPq, false>(a, st);
 }
 

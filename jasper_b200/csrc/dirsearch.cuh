@@ -5,7 +5,7 @@
 
 namespace jb {
 
-enum DirKind : int { kDirLsh = 0, kDirPq = 1, kDirRabitq = 2 };
+enum DirKind : int { kDirLsh = 0, kDirPq = 1 };
 
 struct DirSearchArgs {
   GraphView g;
@@ -23,10 +23,6 @@ struct DirSearchArgs {
   const float* centroids;
   const uint8_t* codes;
   const float* norms;
-  // RaBitQ
-  const uint8_t* rq_store;
-  uint32_t rq_node_bytes, rq_code_bytes;
-  const float* rq_centroid;
   // queries / outputs
   const uint16_t* queries;  // [nq][dpad]
   uint32_t nq, k, bw, limit, max_result_size;

@@ -97,6 +97,7 @@ void graph_free_directional(Graph& g) {
   if (d.rotation_pad) cudaFree(d.rotation_pad);
   if (d.rq_store) cudaFree(d.rq_store);
   if (d.rq_centroid) cudaFree(d.rq_centroid);
+  if (d.rq_err) cudaFree(d.rq_err);
   d = DirArtifacts{};
 }
 

@@ -60,6 +60,7 @@ struct DirArtifacts {
   uint32_t rq_code_bytes = 0, rq_node_bytes = 0;
   uint8_t* rq_store = nullptr;    // [n][rq_node_bytes]: code bits, f_add, f_rescale (f32)
   float* rq_centroid = nullptr;   // [dim] column mean of the rows the codes were made from
+  float* rq_err = nullptr;        // [n] error scale of each row's estimate (search filter)
   bool prerotate = false;
   uint64_t rotation_seed = 0;
   uint16_t* rotation = nullptr;   // [dim][dim] fp16, column-major P (rows rotate as x^T P)

@@ -12,7 +12,9 @@
 //   IP: f_add = 1 - <r, c> + |r|^2 <c, xu> / <r, xu>, f_rescale = -|r| / ipn
 // with xu = code - 1/2 and ipn = sum 0.5 |r_i| / |r|.  The node store is the
 // reference's array of structs (layout.cuh:42-116): ceil(dim / 8) code bytes
-// padded to 4, then f_add and f_rescale as f32.
+// padded to 4, then f_add and f_rescale as f32.  For a graph's own rows the
+// kernel also writes each row's estimate error scale (used by the search's
+// RaBitQ candidate filter; the reference has no such output).
 //
 // jb_rabitq_quantize also restates the reference's rotations in fp32: rows
 // by P^T (rotate_data_vec, OP_T) and the centroid by P (rotate_single_
@@ -55,7 +57,8 @@ __global__ void centroid_kernel(const uint16_t* __restrict__ vec, uint64_t n, ui
 template <typename T>
 __global__ void quantize_kernel(const T* __restrict__ rows, uint64_t n, uint64_t stride,
                                 uint32_t dim, const float* __restrict__ c, int ip,
-                                uint8_t* __restrict__ out, uint32_t code_bytes) {
+                                uint8_t* __restrict__ out, uint32_t code_bytes,
+                                float* __restrict__ err_out) {
   const int lane = threadIdx.x & 31, t = lane & 3;
   const unsigned mask = 0xFu << (lane & ~3);
   const uint64_t tile = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 2;
@@ -104,6 +107,16 @@ __global__ void quantize_kernel(const T* __restrict__ rows, uint64_t n, uint64_t
       }
       reinterpret_cast<float*>(node + code_bytes)[0] = f_add;
       reinterpret_cast<float*>(node + code_bytes)[1] = f_rescale;
+      if (err_out != nullptr) {
+        // error scale of the estimate (the search filter's bound): with
+        // a = <o_bar, o> = 2 ipn / sqrt(dim), the 1-bit estimate of <r, q - c>
+        // has standard error |r| |q - c| sqrt(1 - a^2) / (a sqrt(dim - 1));
+        // stored without |q - c|, times 2 for L2.
+        const float a = __fdiv_rn(__fmul_rn(2.0f, ip_norm), __fsqrt_rn(float(dim)));
+        const float num = __fmul_rn(__fmul_rn(ip ? 1.0f : 2.0f, l2_norm),
+                                    __fsqrt_rn(fmaxf(0.0f, __fsub_rn(1.0f, __fmul_rn(a, a)))));
+        err_out[i] = __fdiv_rn(num, __fmul_rn(a, __fsqrt_rn(float(dim - 1))));
+      }
     }
     for (uint32_t jb = t; jb < code_bytes; jb += 4) {
       uint32_t byte = 0;
@@ -163,7 +176,7 @@ void rabitq_quantize_rows(const float* rows, uint64_t n, uint32_t dim, const flo
     c = rot_c;
   }
   quantize_kernel<float><<<grid_for(n * 4, 256), 256, 0, st>>>(x, n, dim, dim, c, ip, out,
-                                                               rabitq_code_bytes(dim));
+                                                               rabitq_code_bytes(dim), nullptr);
   const cudaError_t e = cudaGetLastError();
   if (rot_rows) cudaFreeAsync(rot_rows, st);
   if (rot_c) cudaFreeAsync(rot_c, st);
@@ -175,16 +188,19 @@ void build_rabitq(Graph& g, cudaStream_t st) {
   DirArtifacts& d = g.dir;
   if (d.rq_store) cudaFree(d.rq_store);
   if (d.rq_centroid) cudaFree(d.rq_centroid);
+  if (d.rq_err) cudaFree(d.rq_err);
   d.rq_store = nullptr;
   d.rq_centroid = nullptr;
+  d.rq_err = nullptr;
   d.rq_code_bytes = rabitq_code_bytes(g.dim);
   d.rq_node_bytes = d.rq_code_bytes + 8;
   check(cudaMalloc(&d.rq_centroid, size_t(g.dim) * 4 + 16), "alloc rabitq centroid");
   check(cudaMalloc(&d.rq_store, size_t(g.n) * d.rq_node_bytes + 16), "alloc rabitq codes");
+  check(cudaMalloc(&d.rq_err, size_t(g.n) * 4 + 16), "alloc rabitq error scales");
   centroid_kernel<<<(g.dim + 127) / 128, 128, 0, st>>>(g.vec, g.n, g.dim, g.dpad, d.rq_centroid);
   quantize_kernel<uint16_t><<<grid_for(uint64_t(g.n) * 4, 256), 256, 0, st>>>(
       g.vec, g.n, g.dpad, g.dim, d.rq_centroid, g.metric == kIP ? 1 : 0, d.rq_store,
-      d.rq_code_bytes);
+      d.rq_code_bytes, d.rq_err);
   check(cudaGetLastError(), "rabitq build launch");
   check(cudaStreamSynchronize(st), "rabitq build");
   d.has_rabitq = true;

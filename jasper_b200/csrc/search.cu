@@ -73,7 +73,7 @@ __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(
 // nq: chunk quads of the lane-per-row instance (template MAXC), 0 for the
 // shared-memory-query instance.
 __host__ __device__ inline size_t warp_smem_bytes(uint32_t bwcap, uint32_t hbits, uint32_t dpad,
-                                                  uint32_t nq) {
+                                                  uint32_t nq, uint32_t rq_words = 0) {
   const bool smem_query = nq == 0;
   size_t b = 0;
   b += 2 * sizeof(uint64_t) * bwcap;
@@ -84,6 +84,7 @@ __host__ __device__ inline size_t warp_smem_bytes(uint32_t bwcap, uint32_t hbits
   // lane-per-row query pairs: 2 * nq chunk pairs x 8 float2
   if (smem_query) b += align16(sizeof(uint16_t) * dpad);
   else b += size_t(128) * nq + 64;  // query pairs, or the tile layout's padded chains
+  b += align16(size_t(rq_words) * 4);  // RaBitQ query bit-planes (filter on)
   return b;
 }
 
@@ -114,16 +115,28 @@ __device__ __forceinline__ bool hash_insert(uint32_t* h, uint32_t hbits, uint32_
   return true;
 }
 
-// Shared-memory query: any dpad, L2 or inner product.
+// Shared-memory query: any dpad, L2 or inner product.  Loads are issued in
+// batches of eight chunks before they are consumed (the accumulation order
+// is unchanged: chunks s, s+4, ... for L2, every chunk in order for IP).
 template <int METRIC>
 __device__ __forceinline__ float dist_smemq(const uint16_t* qs, const uint4* row, bool active,
                                             int nchunks, int s) {
+  constexpr int B = 8;
   float acc = 0.f;
   if (METRIC == kL2) {
     const uint4* q4 = reinterpret_cast<const uint4*>(qs);
-    for (int c = s; c < nchunks; c += 4) {
-      uint4 r = active ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
-      acc = l2_chunk(q4[c], r, acc);
+    for (int c0 = s; c0 < nchunks; c0 += 4 * B) {
+      uint4 r[B];
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const int c = c0 + 4 * u;
+        r[u] = (active && c < nchunks) ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const int c = c0 + 4 * u;
+        if (c < nchunks) acc = l2_chunk(q4[c], r[u], acc);
+      }
     }
   } else {
     // element i belongs to lane i % 4: in chunk c lane s takes elements s and
@@ -131,10 +144,20 @@ __device__ __forceinline__ float dist_smemq(const uint16_t* qs, const uint4* row
     const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qs);
     const uint32_t* r32 = reinterpret_cast<const uint32_t*>(row);
     const int w = s >> 1;
-    for (int c = 0; c < nchunks; c++) {
-      uint32_t rlo = active ? __ldg(r32 + 4 * c + w) : 0u;
-      uint32_t rhi = active ? __ldg(r32 + 4 * c + 2 + w) : 0u;
-      acc = ip_pair(q32[4 * c + w], q32[4 * c + 2 + w], rlo, rhi, s, acc);
+    for (int c0 = 0; c0 < nchunks; c0 += B) {
+      uint32_t lo[B], hi[B];
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const int c = c0 + u;
+        const bool ok = active && c < nchunks;
+        lo[u] = ok ? __ldg(r32 + 4 * c + w) : 0u;
+        hi[u] = ok ? __ldg(r32 + 4 * c + 2 + w) : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const int c = c0 + u;
+        if (c < nchunks) acc = ip_pair(q32[4 * c + w], q32[4 * c + 2 + w], lo[u], hi[u], s, acc);
+      }
     }
   }
   acc = tile4_sum(acc);
@@ -303,6 +326,36 @@ __device__ __forceinline__ float2 tile4_pair_chain(const float* qs, const uint4 
   return acc;
 }
 
+// RaBitQ estimate of the distance to node l (no reference counterpart):
+// est = f_add + f_rescale * <code - 1/2, q~> + gadd (IP: minus 1), with
+// <code - 1/2, q~> = 0.5 vl (2 popc(b) - dim) + 0.5 delta (2 A - S) and
+// A = sum_p 2^p popc(b & plane_p) over the query's 4 bit-planes.
+__device__ __forceinline__ float rabitq_est(const SearchArgs& a, uint32_t l, const uint32_t* planes,
+                                            uint32_t nw, uint32_t dim, float vl, float delta, int S,
+                                            float gadd, bool ip) {
+  const uint8_t* node = a.rq_store + size_t(l) * a.rq_node_bytes;
+  const uint32_t* cw = reinterpret_cast<const uint32_t*>(node);
+  int A = 0, pb = 0;
+  for (uint32_t w = 0; w < nw; w++) {
+    const uint32_t b = __ldg(cw + w);
+    pb += __popc(b);
+    A += __popc(b & planes[w]) + (__popc(b & planes[nw + w]) << 1) +
+         (__popc(b & planes[2 * nw + w]) << 2) + (__popc(b & planes[3 * nw + w]) << 3);
+  }
+  const float f_add = __ldg(reinterpret_cast<const float*>(node + a.rq_code_bytes));
+  const float f_rescale = __ldg(reinterpret_cast<const float*>(node + a.rq_code_bytes) + 1);
+  const float t1 = __fmul_rn(float(2 * pb - int(dim)), __fmul_rn(0.5f, vl));
+  const float ipx = __fmaf_rn(float(2 * A - S), __fmul_rn(0.5f, delta), t1);
+  const float est = __fadd_rn(__fmaf_rn(f_rescale, ipx, f_add), gadd);
+  return ip ? __fsub_rn(est, 1.0f) : est;
+}
+
+__device__ __forceinline__ float warp_sum_xor(float v) {
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) v = __fadd_rn(v, __shfl_xor_sync(kFull, v, d));
+  return v;
+}
+
 #ifndef JB_SEARCH_MIN_BLOCKS
 #define JB_SEARCH_MIN_BLOCKS 4
 #endif
@@ -333,8 +386,11 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC>())
   const int lane = threadIdx.x & 31;
   const int wid = threadIdx.x >> 5;
   const uint32_t dpad = a.g.dpad;
-  const size_t per_warp = warp_smem_bytes(BWCAP, HBITS, dpad, MAXC);
+  const uint32_t rq_nw = a.rq_on ? (a.g.dim + 31) / 32 : 0;
+  const size_t per_warp = warp_smem_bytes(BWCAP, HBITS, dpad, MAXC, 4 * rq_nw);
   WarpSmem sm = carve(smem_raw + per_warp * wid, BWCAP, HBITS);
+  uint32_t* rq_planes = reinterpret_cast<uint32_t*>(smem_raw + per_warp * wid + per_warp -
+                                                    align16(size_t(4) * rq_nw * 4));
   const int tile = lane >> 2, s = lane & 3;
   const int nchunks = int(dpad / 8);
   const GraphView& g = a.g;
@@ -364,6 +420,58 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC>())
       for (int c = lane; c < nchunks; c += 32) dst[c] = ldg16(src + c);
     }
     for (uint32_t i = lane; i < hsize; i += 32) sm.hash[i] = kHashEmpty;
+    // RaBitQ filter: the query's 4-bit planes, offsets and centroid terms.
+    float rq_vl = 0.0f, rq_delta = 0.0f, rq_gadd = 0.0f, rq_lq = 0.0f;
+    int rq_S = 0;
+    if (a.rq_on) {
+      const __half* qv = reinterpret_cast<const __half*>(qrow);
+      const uint32_t dim = g.dim;
+      float vl = __int_as_float(0x7F800000), vr = -vl;
+      for (uint32_t i = lane; i < dim; i += 32) {
+        const float x = __half2float(qv[i]);
+        vl = fminf(vl, x);
+        vr = fmaxf(vr, x);
+      }
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) {
+        vl = fminf(vl, __shfl_xor_sync(kFull, vl, d));
+        vr = fmaxf(vr, __shfl_xor_sync(kFull, vr, d));
+      }
+      const float range = __fsub_rn(vr, vl);
+      const float inv = range > 0.0f ? __fdiv_rn(15.0f, range) : 0.0f;
+      int S = 0;
+      for (uint32_t w = 0; w < rq_nw; w++) {
+        const uint32_t i = 32 * w + lane;
+        int qq = 0;
+        if (i < dim) {
+          qq = __float2int_rn(__fmul_rn(__fsub_rn(__half2float(qv[i]), vl), inv));
+          qq = qq < 0 ? 0 : (qq > 15 ? 15 : qq);
+        }
+        S += qq;
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+          const uint32_t bits = __ballot_sync(kFull, (qq >> p) & 1);
+          if (lane == 0) rq_planes[p * rq_nw + w] = bits;
+        }
+      }
+#pragma unroll
+      for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(kFull, S, d);
+      float acc_ip = 0.0f, acc_l2 = 0.0f;
+      for (uint32_t i = lane; i < dim; i += 32) {
+        const float x = __half2float(qv[i]);
+        const float ci = __ldg(a.rq_centroid + i);
+        acc_ip = __fmaf_rn(ci, x, acc_ip);
+        const float dd = __fsub_rn(x, ci);
+        acc_l2 = __fmaf_rn(dd, dd, acc_l2);
+      }
+      acc_ip = warp_sum_xor(acc_ip);
+      acc_l2 = warp_sum_xor(acc_l2);
+      rq_vl = vl;
+      rq_delta = __fdiv_rn(range, 15.0f);
+      rq_S = S;
+      rq_gadd = METRIC == kIP ? -acc_ip : acc_l2;
+      rq_lq = __fmul_rn(a.rq_margin, __fsqrt_rn(acc_l2));
+    }
     __syncwarp();
 
     uint32_t first_evals = 0;  // per lane; summed at the end (stats only)
@@ -554,11 +662,38 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC>())
       const uint32_t lt = (1u << lane) - 1u;
       if (f0) sm.cand_ids[__popc(b0 & lt)] = nb0;
       if (f1) sm.cand_ids[__popc(b0) + __popc(b1 & lt)] = nb1;
-      const int m = __popc(b0) + __popc(b1);
+      int m = __popc(b0) + __popc(b1);
       n_hash += m;
       __syncwarp();
       JB_CLK(2)
       if (m == 0) continue;
+      if (a.rq_on && cnt == bw) {
+        // RaBitQ filter: drop candidates that cannot enter the full beam.
+        const float tau = key_dist(cur[bw - 1]);
+        bool k0 = false, k1 = false;
+        uint32_t c0 = 0, c1 = 0;
+        if (lane < m) {
+          c0 = sm.cand_ids[lane];
+          const uint32_t l = c0 - g.global_offset;
+          const float est = rabitq_est(a, l, rq_planes, rq_nw, g.dim, rq_vl, rq_delta, rq_S,
+                                       rq_gadd, METRIC == kIP);
+          k0 = !(__fsub_rn(est, __fmul_rn(rq_lq, __ldg(a.rq_err + l))) > tau);
+        }
+        if (lane + 32 < m) {
+          c1 = sm.cand_ids[lane + 32];
+          const uint32_t l = c1 - g.global_offset;
+          const float est = rabitq_est(a, l, rq_planes, rq_nw, g.dim, rq_vl, rq_delta, rq_S,
+                                       rq_gadd, METRIC == kIP);
+          k1 = !(__fsub_rn(est, __fmul_rn(rq_lq, __ldg(a.rq_err + l))) > tau);
+        }
+        const uint32_t kb0 = __ballot_sync(kFull, k0), kb1 = __ballot_sync(kFull, k1);
+        __syncwarp();
+        if (k0) sm.cand_ids[__popc(kb0 & lt)] = c0;
+        if (k1) sm.cand_ids[__popc(kb0) + __popc(kb1 & lt)] = c1;
+        m = __popc(kb0) + __popc(kb1);
+        __syncwarp();
+        if (m == 0) continue;
+      }
       evals += m;
       const int kept = evaluate_and_sort(m);
       if (kept == 0) continue;
@@ -648,7 +783,8 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC>())
 template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC>
 void launch_t(const SearchArgs& a, cudaStream_t stream) {
   auto kern = beam_search_warp_kernel<BWCAP, HBITS, MAXC, METRIC>;
-  const size_t per_warp = warp_smem_bytes(BWCAP, HBITS, a.g.dpad, MAXC);
+  const size_t per_warp =
+      warp_smem_bytes(BWCAP, HBITS, a.g.dpad, MAXC, a.rq_on ? 4 * ((a.g.dim + 31) / 32) : 0);
   int wpb = 4;
   while (wpb > 1 && per_warp * wpb > 200 * 1024) wpb--;
   if (per_warp * wpb > 220 * 1024) throw std::runtime_error("search: shared memory per query too large");

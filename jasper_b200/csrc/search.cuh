@@ -27,6 +27,15 @@ struct SearchArgs {
                            // visited-table resets, first-time distance evals
   uint32_t* seen_bits;     // optional zeroed [nq][ceil(n / 32)] bitmap; with it stats[4]
                            // counts each distinct row once (the roofline's numerator)
+  // Optional RaBitQ candidate filter (rq_on): with the beam full, a new
+  // neighbour whose estimate minus rq_margin * |q - c| * rq_err[v] exceeds
+  // the beam's worst exact distance is skipped without reading its row.
+  int rq_on;
+  const uint8_t* rq_store;   // [n][rq_node_bytes]: code bits, f_add, f_rescale
+  uint32_t rq_node_bytes, rq_code_bytes;
+  const float* rq_centroid;  // [dim]
+  const float* rq_err;       // [n]
+  float rq_margin;
 };
 
 // Bytes of device scratch a search launch needs (the work counter).

@@ -226,11 +226,42 @@ static int is_deleted(const orc_graph *g, uint32_t gid) {
  * slots get (UINT32_MAX, 1e30f) (beam_search.cuh:218-221).  When `visited`
  * is non-NULL records the expansion order (beam_search.cuh:157-166).
  * Returns the number of expansions. */
+static void rabitq_query_prep(const uint16_t *q, uint32_t dim, const float *c, int ip,
+                              uint32_t *planes, float *vl_out, float *delta_out, int *S_out,
+                              float *gadd_out, float *qcn_out);
+static float rabitq_estimate(const uint8_t *node, uint32_t code_bytes, uint32_t dim,
+                             const uint32_t *planes, float vl, float delta, int S, float gadd,
+                             int ip);
+
+/* RaBitQ candidate filter of the exact beam search (no reference
+ * counterpart): with the beam full, a new neighbour v is skipped -- its row
+ * never read -- when est(v) - margin * |q - c| * err(v) > the beam's worst
+ * exact distance; otherwise the search is the reference's exactly. */
+typedef struct {
+  const uint8_t *store;     /* [n][node_bytes]: code bits, f_add, f_rescale */
+  uint32_t node_bytes, code_bytes;
+  const float *centroid;    /* [dim] */
+  const float *err;         /* [n] */
+  float margin;
+} orc_rq;
+
+static const orc_rq *g_rq = NULL;  /* filter for orc_search_one (test infrastructure) */
+
 uint32_t orc_search_one(const orc_graph *g, const uint16_t *q, uint32_t k,
                         uint32_t bw, uint32_t limit, uint32_t max_result_size,
                         uint32_t *out_idx, float *out_dist,
                         uint32_t *visited_idx, float *visited_dist,
                         uint64_t *n_dist_evals) {
+  const orc_rq *rq = g_rq;
+  uint32_t *rq_planes = NULL;
+  float rq_vl = 0.f, rq_delta = 0.f, rq_gadd = 0.f, rq_qcn = 0.f, rq_lq = 0.f;
+  int rq_S = 0;
+  if (rq) {
+    rq_planes = (uint32_t *)calloc((size_t)4 * ((g->dim + 31) / 32), sizeof(uint32_t));
+    rabitq_query_prep(q, g->dim, rq->centroid, g->metric == 1, rq_planes, &rq_vl, &rq_delta,
+                      &rq_S, &rq_gadd, &rq_qcn);
+    rq_lq = rq->margin * rq_qcn;
+  }
   uint32_t cap = bw + 64 + 64;
   orc_entry *buf = (orc_entry *)malloc(sizeof(orc_entry) * cap);
   orc_entry *tmp = (orc_entry *)malloc(sizeof(orc_entry) * cap);
@@ -258,14 +289,24 @@ uint32_t orc_search_one(const orc_graph *g, const uint16_t *q, uint32_t k,
     uint32_t u = buf[f].idx;
     uint32_t ne = g->counts[u - g->global_offset];
     uint32_t off = count;
+    const int filter = rq != NULL && count >= bw;
+    const float tau = filter ? buf[bw - 1].dist : 0.0f;
+    uint32_t added = 0;
     for (uint32_t i = 0; i < ne; i++) {
       uint32_t nb = g->edges[(size_t)(u - g->global_offset) * g->R + i];
       orc_entry e;
       if (nb >= lo && nb < hi) { e.idx = nb; e.dist = 3.402823466e+38f; e.visited = 0; }
       else { e.idx = ORC_EMPTY_IDX; e.dist = 3.402823466e+38f; e.visited = 1; }
-      buf[off + i] = e;
+      if (filter && e.idx != ORC_EMPTY_IDX) {
+        const size_t l = nb - g->global_offset;
+        const float est = rabitq_estimate(rq->store + l * rq->node_bytes, rq->code_bytes, g->dim,
+                                          rq_planes, rq_vl, rq_delta, rq_S, rq_gadd,
+                                          g->metric == 1);
+        if (est - rq_lq * rq->err[l] > tau) continue;
+      }
+      buf[off + added++] = e;
     }
-    count += ne;
+    count += added;
     /* populate_distances from offset (device_kernels.cuh:23-57) */
     for (uint32_t i = off; i < count; i++) {
       if (buf[i].idx != ORC_EMPTY_IDX) {
@@ -298,8 +339,18 @@ uint32_t orc_search_one(const orc_graph *g, const uint16_t *q, uint32_t k,
   for (; out < k; out++) { out_idx[out] = ORC_INVALID; out_dist[out] = 1e30f; }
   free(buf);
   free(tmp);
+  free(rq_planes);
   if (n_dist_evals) *n_dist_evals = evals;
   return visited_counter;
+}
+
+void orc_set_rabitq_filter(const uint8_t *store, uint32_t node_bytes, const float *centroid,
+                           const float *err, float margin, int enable) {
+  static orc_rq rq;
+  if (!enable) { g_rq = NULL; return; }
+  rq.store = store; rq.node_bytes = node_bytes; rq.code_bytes = node_bytes - 8;
+  rq.centroid = centroid; rq.err = err; rq.margin = margin;
+  g_rq = &rq;
 }
 
 /* Batch of independent queries (one CUDA block each in the reference). */
@@ -647,9 +698,6 @@ typedef struct {
   const float *centroids;   /* [M][256][dsub] */
   const uint8_t *codes;     /* [n][M * R] subspace-major */
   const float *norms;       /* [n] */
-  const uint8_t *rq_store;  /* RaBitQ: [n][node_bytes] {code bits, f_add, f_rescale} */
-  uint32_t rq_node_bytes, rq_code_bytes;
-  const float *rq_centroid; /* [dim], rotated space */
 } orc_dir;
 
 /* compute_qu_diff_and_exact (beam_search_common.cuh:87-154); fills qu (fp16
@@ -714,7 +762,7 @@ static void fr_insert(orc_entry *fr, uint32_t *fc, uint32_t k, uint32_t idx, flo
  *   over 32 lanes (i = l, l + 32, ...; fma) and reduced by the warp butterfly. */
 static void rabitq_query_prep(const uint16_t *q, uint32_t dim, const float *c, int ip,
                               uint32_t *planes, float *vl_out, float *delta_out, int *S_out,
-                              float *gadd_out) {
+                              float *gadd_out, float *qcn_out) {
   float vl = orc_half_to_float(q[0]), vr = vl;
   for (uint32_t i = 1; i < dim; i++) {
     float x = orc_half_to_float(q[i]);
@@ -745,8 +793,18 @@ static void rabitq_query_prep(const uint16_t *q, uint32_t dim, const float *c, i
     v[l] = acc;
   }
   float gsum = warp_reduce32(v);
+  for (int l = 0; l < 32; l++) {
+    float acc = 0.f;
+    for (uint32_t i = (uint32_t)l; i < dim; i += 32) {
+      float d = orc_half_to_float(q[i]) - c[i];
+      acc = fmaf(d, d, acc);
+    }
+    v[l] = acc;
+  }
+  float qc2 = warp_reduce32(v);
   *vl_out = vl; *delta_out = delta; *S_out = S;
   *gadd_out = ip ? -gsum : gsum;
+  *qcn_out = sqrtf(qc2);
 }
 
 /* est = f_add + f_rescale * <code - 1/2, q~> + gadd (IP: minus 1, the
@@ -779,7 +837,7 @@ static float rabitq_estimate(const uint8_t *node, uint32_t code_bytes, uint32_t 
  * (mask 2 then 1); code bit = r >= 0; f_add / f_rescale as the reference
  * writes them.  Output: the reference's array-of-structs node layout. */
 static void rabitq_row(const float *x, const float *c, uint32_t dim, int ip, uint8_t *node,
-                       uint32_t code_bytes) {
+                       uint32_t code_bytes, float *err) {
   float part[4] = {0, 0, 0, 0};
   for (uint32_t j = 0; j < dim; j++) { float r = x[j] - c[j]; part[j % 4] = fmaf(r, r, part[j % 4]); }
   const float l2_sqr = (part[0] + part[2]) + (part[1] + part[3]);
@@ -818,21 +876,32 @@ static void rabitq_row(const float *x, const float *c, uint32_t dim, int ip, uin
   }
   memcpy(node + code_bytes, &f_add, 4);
   memcpy(node + code_bytes + 4, &f_rescale, 4);
+  if (err) {
+    /* error scale of the estimate (no reference counterpart): with
+     * a = <o_bar, o> = 2 ipn / sqrt(dim), the 1-bit estimate of <r, q - c>
+     * has standard error |r| |q - c| sqrt(1 - a^2) / (a sqrt(dim - 1)); err
+     * holds that without |q - c|, times 2 for L2 (the term enters as -2<r, q>). */
+    const float a = (2.0f * ip_norm) / sqrtf((float)dim);
+    const float num = (ip ? 1.0f : 2.0f) * l2_norm * sqrtf(fmaxf(0.0f, 1.0f - a * a));
+    *err = num / (a * sqrtf((float)(dim - 1)));
+  }
 }
 
 uint32_t orc_rabitq_code_bytes(uint32_t dim) { return ((dim + 7) / 8 + 3) / 4 * 4; }
 
-typedef struct { const float *rows; uint64_t stride; const float *c; uint32_t dim; int ip; uint8_t *out; } rq_ctx;
+typedef struct { const float *rows; uint64_t stride; const float *c; uint32_t dim; int ip; uint8_t *out; float *err; } rq_ctx;
 
 static void rq_body(void *vctx, long i) {
   rq_ctx *c = (rq_ctx *)vctx;
   const uint32_t cb = orc_rabitq_code_bytes(c->dim);
-  rabitq_row(c->rows + (size_t)i * c->stride, c->c, c->dim, c->ip, c->out + (size_t)i * (cb + 8), cb);
+  rabitq_row(c->rows + (size_t)i * c->stride, c->c, c->dim, c->ip, c->out + (size_t)i * (cb + 8), cb,
+             c->err ? c->err + i : NULL);
 }
 
+/* err may be NULL (the reference's quantizer has no error output). */
 void orc_rabitq_quantize(const float *rows, uint64_t n, uint64_t stride, uint32_t dim,
-                         const float *centroid, int ip, uint8_t *out) {
-  rq_ctx c = {rows, stride, centroid, dim, ip, out};
+                         const float *centroid, int ip, uint8_t *out, float *err) {
+  rq_ctx c = {rows, stride, centroid, dim, ip, out, err};
   parallel_for((long)n, rq_body, &c);
 }
 
@@ -863,15 +932,7 @@ void orc_dir_search_one(const orc_graph *g, const orc_dir *dd, const uint16_t *q
   float q_sq = 0.f, inv_nd = 0.f;
   uint32_t fc = 0, count = 1;
   buf[0].idx = g->medoid; buf[0].dist = 0.0f; buf[0].visited = 0;
-  /* RaBitQ query state: 4-bit query planes, offsets, centroid term */
-  uint32_t *rq_planes = NULL;
-  float rq_vl = 0.f, rq_delta = 0.f, rq_gadd = 0.f;
-  int rq_S = 0;
-  if (dd->kind == 2) {
-    const uint32_t dim = g->dim, nw = (dim + 31) / 32;
-    rq_planes = (uint32_t *)calloc((size_t)4 * nw, sizeof(uint32_t));
-    rabitq_query_prep(q, dim, dd->rq_centroid, ip, rq_planes, &rq_vl, &rq_delta, &rq_S, &rq_gadd);
-  } else if (dd->kind == 0) {
+  if (dd->kind == 0) {
     inv_nd = 1.0f / dd->norm_denom;
   } else {
     const uint32_t M = dd->pq_m, dsub = dd->pq_dsub;
@@ -907,7 +968,7 @@ void orc_dir_search_one(const orc_graph *g, const orc_dir *dd, const uint16_t *q
     buf[f].visited = 1;
     const uint32_t u = buf[f].idx;
     float exact_u, dist_u;
-    if (dd->kind == 0 || dd->kind == 2) {
+    if (dd->kind == 0) {
       exact_u = dir_visit_exact(g, q, u, ip, ip ? NULL : qu);
       dist_u = ip ? -exact_u : exact_u;
     } else {
@@ -932,11 +993,7 @@ void orc_dir_search_one(const orc_graph *g, const orc_dir *dd, const uint16_t *q
       orc_entry *en = &buf[off + e];
       if (en->idx == ORC_EMPTY_IDX) continue;
       float est;
-      if (dd->kind == 2) {
-        est = rabitq_estimate(dd->rq_store + (size_t)(en->idx - g->global_offset) * dd->rq_node_bytes,
-                              dd->rq_code_bytes, g->dim, rq_planes, rq_vl, rq_delta, rq_S,
-                              rq_gadd, ip);
-      } else if (dd->kind == 0) {
+      if (dd->kind == 0) {
         float dot = 0.f;
         for (uint32_t r = 0; r < dd->k_ranks; r++) {
           uint32_t word, coord, neg;
@@ -986,7 +1043,7 @@ void orc_dir_search_one(const orc_graph *g, const orc_dir *dd, const uint16_t *q
     out_idx[out] = idx; out_dist[out] = fr[i].dist; out++;
   }
   for (; out < k; out++) { out_idx[out] = ORC_EMPTY_IDX; out_dist[out] = 3.402823466e+38f; }
-  free(buf); free(tmp); free(fr); free(qu); free(lut); free(rq_planes);
+  free(buf); free(tmp); free(fr); free(qu); free(lut);
 }
 
 typedef struct {

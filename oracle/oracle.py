@@ -183,8 +183,6 @@ class _Dir(C.Structure):
         ("packed", C.c_void_p), ("mag_sq", C.c_void_p), ("c", C.c_void_p),
         ("norm_denom", C.c_float), ("pq_m", C.c_uint32), ("pq_dsub", C.c_uint32),
         ("centroids", C.c_void_p), ("codes", C.c_void_p), ("norms", C.c_void_p),
-        ("rq_store", C.c_void_p), ("rq_node_bytes", C.c_uint32), ("rq_code_bytes", C.c_uint32),
-        ("rq_centroid", C.c_void_p),
     ]
 
 
@@ -196,8 +194,7 @@ def set_dir_mode(m: int) -> None:
 
 def dir_search(g: OracleGraph, kind: str, art: dict, queries: np.ndarray, k: int,
                beam_width: int, limit: int):
-    """directional_search ('lsh'), pq_search ('pq') or the RaBitQ-estimated
-    search ('rabitq') given the artifacts."""
+    """directional_search ('lsh') or pq_search ('pq') given the artifacts."""
     L = lib()
     L.orc_dir_search.argtypes = [C.POINTER(_Graph), C.POINTER(_Dir), C.c_void_p, C.c_uint32,
                                  C.c_uint32, C.c_uint32, C.c_uint32, C.c_void_p, C.c_void_p]
@@ -208,15 +205,7 @@ def dir_search(g: OracleGraph, kind: str, art: dict, queries: np.ndarray, k: int
         keep[name] = a
         return _p(a)
     d = _Dir()
-    if kind == "rabitq":
-        store = np.ascontiguousarray(art["rq_store"], np.uint8)
-        keep["store"] = store
-        d.kind = 2
-        d.rq_store = _p(store)
-        d.rq_node_bytes = store.shape[1]
-        d.rq_code_bytes = store.shape[1] - 8
-        d.rq_centroid = arr("rq_centroid", np.float32)
-    elif kind == "lsh":
+    if kind == "lsh":
         packed = np.ascontiguousarray(art["lsh_packed"])
         keep["packed"] = packed
         d.kind, d.k_ranks, d.packed_bytes = 0, int(art["k_ranks"]), packed.dtype.itemsize
@@ -281,19 +270,34 @@ def rabitq_code_bytes(dim: int) -> int:
     return ((dim + 7) // 8 + 3) // 4 * 4
 
 
-def rabitq_quantize(rows: np.ndarray, centroid: np.ndarray, ip: bool) -> np.ndarray:
+def rabitq_quantize(rows: np.ndarray, centroid: np.ndarray, ip: bool, with_err: bool = False):
     """rabitq_quantize_kernel<1> restated: rows [n, dim] float32 (already
-    rotated) -> node store [n, code_bytes + 8] uint8."""
+    rotated) -> node store [n, code_bytes + 8] uint8 (and, with_err, the
+    per-row error scale of the estimate used by the search filter)."""
     L = lib()
     L.orc_rabitq_quantize.argtypes = [C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint32, C.c_void_p,
-                                      C.c_int, C.c_void_p]
+                                      C.c_int, C.c_void_p, C.c_void_p]
     L.orc_rabitq_quantize.restype = None
     x = np.ascontiguousarray(rows, np.float32)
     n, dim = x.shape
     c = np.ascontiguousarray(centroid, np.float32)
     out = np.zeros((n, rabitq_code_bytes(dim) + 8), np.uint8)
-    L.orc_rabitq_quantize(_p(x), n, dim, dim, _p(c), int(bool(ip)), _p(out))
-    return out
+    err = np.zeros(n, np.float32) if with_err else None
+    L.orc_rabitq_quantize(_p(x), n, dim, dim, _p(c), int(bool(ip)), _p(out), _p(err))
+    return (out, err) if with_err else out
+
+
+def set_rabitq_filter(store=None, centroid=None, err=None, margin: float = 0.0) -> None:
+    """Make OracleGraph.search apply the RaBitQ candidate filter (None: off).
+    The arrays must stay alive while it is set."""
+    L = lib()
+    L.orc_set_rabitq_filter.argtypes = [C.c_void_p, C.c_uint32, C.c_void_p, C.c_void_p, C.c_float,
+                                        C.c_int]
+    L.orc_set_rabitq_filter.restype = None
+    if store is None:
+        L.orc_set_rabitq_filter(None, 0, None, None, 0.0, 0)
+        return
+    L.orc_set_rabitq_filter(_p(store), store.shape[1], _p(centroid), _p(err), float(margin), 1)
 
 
 def rabitq_centroid(g: "OracleGraph") -> np.ndarray:

@@ -70,8 +70,23 @@ CASES = [
 ]
 
 
+def search_rabitq(h, Q, k, bw, limit, margin, stats=False):
+    import torch
+    q = torch.from_numpy(O.pad_rows(Q)).cuda()
+    nq = q.shape[0]
+    oi = torch.empty(nq, k, dtype=torch.int32, device="cuda")
+    od = torch.empty(nq, k, dtype=torch.float32, device="cuda")
+    st = torch.zeros(nq, 5, dtype=torch.int32, device="cuda") if stats else None
+    _lib.call("jb_graph_search_rabitq", h, q.data_ptr(), nq, q.shape[1], oi.data_ptr(),
+              od.data_ptr(), k, bw, limit, float(margin), None if st is None else st.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    out = (oi.cpu().numpy(), od.cpu().numpy())
+    return out + (st.cpu().numpy(),) if stats else out
+
+
 @pytest.mark.parametrize("case", CASES, ids=lambda c: f"{c[0]}-d{c[2]}-R{c[3]}-m{c[4]}-rot{int(c[5])}")
-def test_rabitq_search_matches_oracle(cuda, case):
+def test_rabitq_filtered_search_matches_oracle(cuda, case):
     kind, n, dim, R, metric, prerotate = case
     gen = getattr(synthetic, kind)
     X = gen(n, dim, 81)
@@ -85,32 +100,33 @@ def test_rabitq_search_matches_oracle(cuda, case):
         _lib.call("jb_graph_get_rabitq", h, C.byref(nb), None, None)
         store = np.zeros((n, nb.value), np.uint8)
         cent = np.zeros(dim, np.float32)
+        err = np.zeros(n, np.float32)
         _lib.call("jb_graph_get_rabitq", h, None, store.ctypes.data, cent.ctypes.data)
-        # codes of the stored rows around their column mean: bit-exact
+        _lib.call("jb_graph_get_rabitq_err", h, err.ctypes.data)
+        # codes and error scales of the stored rows around their column mean: bit-exact
         np.testing.assert_array_equal(cent.view(np.uint32), O.rabitq_centroid(g).view(np.uint32))
         rows = g.vec.view(np.float16)[:, :dim].astype(np.float32)
-        np.testing.assert_array_equal(store, O.rabitq_quantize(rows, cent, metric == 1))
-        art = dict(rq_store=store, rq_centroid=cent)
-        if prerotate:
-            P = np.zeros(dim * dim, np.float32)
-            _lib.call("jb_rotation_matrix", dim, 4, P.ctypes.data)
-            A = P.reshape(dim, dim).astype(np.float16).astype(np.float32)
-            Qs = T.rotate_on_device(Q, dim, 4)   # queries rotated by the same device GEMM
-        else:
-            Qs = Q
-        for k, bw, limit in [(10, 64, 128), (10, 128, 256), (20, 32, 64)]:
-            oi, od = O.dir_search(g, "rabitq", art, Qs, k, bw, limit)
-            if prerotate:
-                ji, jd = T.dir_search_kind(h, 2, Q, k, bw, limit)
-            else:
-                ji, jd = T.dir_search_kind(h, 2, Q, k, bw, limit)
-            T.assert_same_results(ji, jd, oi, od, msg=f"k={k} bw={bw}")
-        # quality: recall@10 at bw 128 against exact neighbours (in the
-        # rotated space the graph holds), near the plain graph search's
+        ost, oerr = O.rabitq_quantize(rows, cent, metric == 1, with_err=True)
+        np.testing.assert_array_equal(store, ost)
+        np.testing.assert_array_equal(err.view(np.uint32), oerr.view(np.uint32))
+        Qs = T.rotate_on_device(Q, dim, 4) if prerotate else Q   # the search's own query rotation
+        try:
+            for margin in (0.0, 1.0, 3.0):
+                O.set_rabitq_filter(store, cent, err, margin)
+                for k, bw, limit in [(10, 64, 128), (10, 128, 256), (20, 32, 64)]:
+                    oi, od, _, oev = g.search(Qs, k, bw, limit)
+                    ji, jd = search_rabitq(h, Q, k, bw, limit, margin)
+                    T.assert_same_results(ji, jd, oi, od, msg=f"margin={margin} k={k} bw={bw}")
+        finally:
+            O.set_rabitq_filter(None)
+        # the filter keeps the exact search's recall at margin 1 with fewer row reads
         gt, _ = O.bruteforce(g.vec.view(np.float16)[:, :dim], Qs, 10, metric)
-        ji, _ = T.dir_search_kind(h, 2, Q, 10, 128, 256)
-        rec = np.mean([len(set(a) & set(b)) / 10 for a, b in zip(ji, gt)])
-        assert rec > 0.8, rec
+        pi, pd = T.search(h, Qs, 10, 128)
+        ri, rd, st = search_rabitq(h, Q, 10, 128, 256, 1.0, stats=True)
+        _, _, pst = T.search(h, Qs, 10, 128, stats=True)
+        rec = lambda ids: np.mean([len(set(a) & set(b)) / 10 for a, b in zip(ids, gt)])
+        assert rec(ri) >= rec(pi) - 0.01, (rec(ri), rec(pi))
+        assert st[:, 2].sum() < pst[:, 2].sum(), (st[:, 2].sum(), pst[:, 2].sum())
     finally:
         T.free(h)
 
@@ -123,6 +139,10 @@ def test_python_rabitq_surface(cuda):
     g = jasper.Graph.build(X, n_neighbors=64, distance="ip", alpha=1.0, build_rabitq=True)
     ids, d = g.rabitq_search(Q, k=10, beam_width=128)
     assert ids.shape == (50, 10) and ids.dtype == torch.int32
+    from oracle import oracle as O2
+    gt, _ = O2.bruteforce(X.cpu().numpy(), Q.cpu().numpy(), 10, 1)
+    rec = np.mean([len(set(a) & set(b)) / 10 for a, b in zip(ids.cpu().numpy(), gt)])
+    assert rec > 0.9, rec
     with pytest.raises(RuntimeError, match="build_lsh"):
         g.directional_search(Q)
     g.free()
