@@ -115,9 +115,10 @@ __device__ __forceinline__ bool hash_insert(uint32_t* h, uint32_t hbits, uint32_
   return true;
 }
 
-// Shared-memory query: any dpad, L2 or inner product.  Loads are issued in
-// batches of eight chunks before they are consumed (the accumulation order
-// is unchanged: chunks s, s+4, ... for L2, every chunk in order for IP).
+// Shared-memory query: any dpad, L2 or inner product.  Each lane loads whole
+// 16-byte chunks s, s+4, ... in batches of eight before consuming them; the
+// accumulation order is the reference's (chunks s, s+4, ... for L2; every
+// chunk in order for IP, the words exchanged within the 4-lane tile).
 template <int METRIC>
 __device__ __forceinline__ float dist_smemq(const uint16_t* qs, const uint4* row, bool active,
                                             int nchunks, int s) {
@@ -141,27 +142,103 @@ __device__ __forceinline__ float dist_smemq(const uint16_t* qs, const uint4* row
   } else {
     // element i belongs to lane i % 4: in chunk c lane s takes elements s and
     // s + 4, i.e. half (s & 1) of 32-bit words (s >> 1) and 2 + (s >> 1).
+    // Lane s loads whole chunks c = s, s+4, ...; for every chunk, in order,
+    // the tile's lanes take the words they need from the lane holding it.
     const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qs);
-    const uint32_t* r32 = reinterpret_cast<const uint32_t*>(row);
     const int w = s >> 1;
-    for (int c0 = 0; c0 < nchunks; c0 += B) {
-      uint32_t lo[B], hi[B];
+    const int tb = (threadIdx.x & 31) & ~3;
+    for (int c0 = 0; c0 < nchunks; c0 += 4 * B) {
+      uint4 r[B];
 #pragma unroll
       for (int u = 0; u < B; u++) {
-        const int c = c0 + u;
-        const bool ok = active && c < nchunks;
-        lo[u] = ok ? __ldg(r32 + 4 * c + w) : 0u;
-        hi[u] = ok ? __ldg(r32 + 4 * c + 2 + w) : 0u;
+        const int c = c0 + 4 * u + s;
+        r[u] = (active && c < nchunks) ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
       for (int u = 0; u < B; u++) {
-        const int c = c0 + u;
-        if (c < nchunks) acc = ip_pair(q32[4 * c + w], q32[4 * c + 2 + w], lo[u], hi[u], s, acc);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int c = c0 + 4 * u + j;  // warp-uniform
+          if (c < nchunks) {
+            const uint32_t x = __shfl_sync(kFull, r[u].x, tb + j);
+            const uint32_t y = __shfl_sync(kFull, r[u].y, tb + j);
+            const uint32_t z = __shfl_sync(kFull, r[u].z, tb + j);
+            const uint32_t ww = __shfl_sync(kFull, r[u].w, tb + j);
+            acc = ip_pair(q32[4 * c + w], q32[4 * c + 2 + w], w ? y : x, w ? ww : z, s, acc);
+          }
+        }
       }
     }
   }
   acc = tile4_sum(acc);
   return METRIC == kL2 ? acc : -acc;
+}
+
+// Two rows per tile in one loop (independent chains interleaved), each row
+// summed exactly as dist_smemq sums it.
+template <int METRIC>
+__device__ __forceinline__ float2 dist_smemq2(const uint16_t* qs, const uint4* row0, bool a0,
+                                              const uint4* row1, bool a1, int nchunks, int s) {
+  constexpr int B = 4;
+  float acc0 = 0.f, acc1 = 0.f;
+  if (METRIC == kL2) {
+    const uint4* q4 = reinterpret_cast<const uint4*>(qs);
+    for (int c0 = s; c0 < nchunks; c0 += 4 * B) {
+      uint4 x0[B], x1[B];
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const int c = c0 + 4 * u;
+        x0[u] = (a0 && c < nchunks) ? ldg16(row0 + c) : make_uint4(0, 0, 0, 0);
+        x1[u] = (a1 && c < nchunks) ? ldg16(row1 + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const int c = c0 + 4 * u;
+        if (c < nchunks) {
+          const uint4 q = q4[c];
+          acc0 = l2_chunk(q, x0[u], acc0);
+          acc1 = l2_chunk(q, x1[u], acc1);
+        }
+      }
+    }
+  } else {
+    const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qs);
+    const int w = s >> 1;
+    const int tb = (threadIdx.x & 31) & ~3;
+    for (int c0 = 0; c0 < nchunks; c0 += 4 * B) {
+      uint4 x0[B], x1[B];
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+        const int c = c0 + 4 * u + s;
+        x0[u] = (a0 && c < nchunks) ? ldg16(row0 + c) : make_uint4(0, 0, 0, 0);
+        x1[u] = (a1 && c < nchunks) ? ldg16(row1 + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < B; u++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int c = c0 + 4 * u + j;  // warp-uniform
+          if (c < nchunks) {
+            // the source lane sends all four words; each lane keeps its two
+            const uint32_t ql = q32[4 * c + w], qh = q32[4 * c + 2 + w];
+            const uint32_t a_x = __shfl_sync(kFull, x0[u].x, tb + j);
+            const uint32_t a_y = __shfl_sync(kFull, x0[u].y, tb + j);
+            const uint32_t a_z = __shfl_sync(kFull, x0[u].z, tb + j);
+            const uint32_t a_w = __shfl_sync(kFull, x0[u].w, tb + j);
+            const uint32_t b_x = __shfl_sync(kFull, x1[u].x, tb + j);
+            const uint32_t b_y = __shfl_sync(kFull, x1[u].y, tb + j);
+            const uint32_t b_z = __shfl_sync(kFull, x1[u].z, tb + j);
+            const uint32_t b_w = __shfl_sync(kFull, x1[u].w, tb + j);
+            acc0 = ip_pair(ql, qh, w ? a_y : a_x, w ? a_w : a_z, s, acc0);
+            acc1 = ip_pair(ql, qh, w ? b_y : b_x, w ? b_w : b_z, s, acc1);
+          }
+        }
+      }
+    }
+  }
+  acc0 = tile4_sum(acc0);
+  acc1 = tile4_sum(acc1);
+  return METRIC == kL2 ? make_float2(acc0, acc1) : make_float2(-acc0, -acc1);
 }
 
 // ── lane-per-row distances (dpad <= 256) ───────────────────────────────────
@@ -550,8 +627,8 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC>())
         const uint32_t id1 = a1 ? sm.cand_ids[i1] : id0;
         const uint4* r0 = reinterpret_cast<const uint4*>(g.vec + size_t(id0 - g.global_offset) * dpad);
         const uint4* r1 = reinterpret_cast<const uint4*>(g.vec + size_t(id1 - g.global_offset) * dpad);
-        const float d0 = dist_smemq<METRIC>(sm.query, r0, a0, nchunks, s);
-        const float d1 = dist_smemq<METRIC>(sm.query, r1, a1, nchunks, s);
+        const float2 dd = dist_smemq2<METRIC>(sm.query, r0, a0, r1, a1, nchunks, s);
+        const float d0 = dd.x, d1 = dd.y;
         if (s == 0) {
           if (a0) sm.cand_keys[i0] = make_key(d0, id0);
           if (a1) sm.cand_keys[i1] = make_key(d1, id1);

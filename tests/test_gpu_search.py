@@ -42,6 +42,7 @@ CASES = [
     ("gaussian", 2000, 128, 32, 1, 1.0, (64, 128)),
     ("relu_sphere", 2000, 320, 32, 1, 1.0, (64,)),
     ("gaussian", 1500, 512, 64, 0, 1.2, (64,)),
+    ("relu_sphere", 1500, 960, 32, 1, 1.0, (64, 128)),
 ]
 
 
