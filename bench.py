@@ -64,10 +64,30 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+_SAMPLER_SRC = r"""
+import sys, time, pynvml
+pynvml.nvmlInit()
+try:
+    h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1])
+except Exception:
+    h = pynvml.nvmlDeviceGetHandleByIndex(int(sys.argv[2]))
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+period = float(sys.argv[3])
+while True:
+    try:
+        print(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+              pynvml.nvmlDeviceGetCurrentClocksEventReasons(h), flush=True)
+    except Exception:
+        pass
+    time.sleep(period)
+"""
+
+
 class ClockSampler:
-    """SM clock and clock-event reasons sampled through NVML every ~2 ms on a
-    background thread while the timed region runs (NVML reads only; no
-    setting of the GPU is touched)."""
+    """SM clock and clock-event reasons sampled through NVML every ~2 ms by a
+    separate process while the timed region runs (a thread in this process
+    would compete for the GIL with host-timed loops).  NVML reads only; no
+    setting of the GPU is touched."""
 
     REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
                "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
@@ -77,44 +97,44 @@ class ClockSampler:
         self.period = period_s
         self.samples: list[tuple[int, int]] = []
         self.max_mhz = None
-        self.handle = None
-        self._stop = threading.Event()
+        self.proc = None
         self.t = None
 
-    def _open(self):
-        import pynvml
-        pynvml.nvmlInit()
-        props = torch.cuda.get_device_properties(self.device)
-        try:
-            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
-            self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-        except Exception:
-            self.handle = pynvml.nvmlDeviceGetHandleByIndex(self.device.index or 0)
-        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
-        return pynvml
-
-    def _run(self, nv):
-        while True:
+    def _read(self):
+        for line in self.proc.stdout:
+            p = line.split()
             try:
-                mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
-                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                self.samples.append((mhz, rs))
-            except Exception:
+                if p[0] == "max":
+                    self.max_mhz = int(p[1])
+                else:
+                    self.samples.append((int(p[0]), int(p[1])))
+            except (ValueError, IndexError):
                 pass
-            if self._stop.wait(self.period):
-                break
 
     def __enter__(self):
         try:
-            nv = self._open()
-            self.t = threading.Thread(target=self._run, args=(nv,), daemon=True)
+            props = torch.cuda.get_device_properties(self.device)
+            bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+            self.proc = subprocess.Popen(
+                [sys.executable, "-c", _SAMPLER_SRC, bus, str(self.device.index or 0),
+                 str(self.period)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.perf_counter()
+            while not self.samples and time.perf_counter() - t0 < 5.0:   # sampler running
+                time.sleep(0.01)
+            self.samples.clear()   # keep only samples taken inside the timed region
         except Exception:
-            self.t = None
+            self.proc = None
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
         if self.t is not None:
             self.t.join(timeout=1.0)
 
