@@ -33,6 +33,7 @@
 // that, deterministically: existing edges, then sinks in (target, sink) order
 // until the cap; the sinks past the cap are never evaluated.
 #include <cub/device/device_radix_sort.cuh>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 #include "construct.cuh"
@@ -347,6 +348,219 @@ __device__ void prune_and_write(const GraphView& gv, uint32_t self, PruneSmem& s
   __syncwarp();
 }
 
+// ---------------------------------------------------------------------------
+// Gram-filtered RobustPrune for one reverse-edge target (dpad <= 128).
+//
+// The warp stages the nc <= kGramMax candidate rows in shared memory and
+// computes their pairwise dot products G = X X^T with mma.sync m16n8k16
+// (fp16 in, fp32 accumulate), one 16-row block row at a time, lower blocks
+// only.  From G it forms an approximate pair distance
+//     L2: d~ = G_ii + G_jj - 2 G_ij        IP: d~ = -G_ij
+// and tests every kept row j against candidate i at once, one or two kept
+// rows per lane.  The prune decision the reference takes is
+// fl(d(i, j) * alpha) < cd with d(i, j) its tile-order fp32 sum.  With
+// |d(i, j) - d~| <= eps (below), rounding is monotone, so
+//     fl((d~ + eps) * alpha) <  cd  =>  pruned,
+//     fl((d~ - eps) * alpha) >= cd  =>  not pruned by j,
+// and only pairs inside the band are evaluated exactly, in the reference's
+// order (exact_pair_dist).  The decisions, and so the kept list, are the
+// ones prune_and_write takes.
+//
+// eps = 2^-11 (G_ii + G_jj).  Error budget: the fp16 products are exact in
+// fp32; one m16n8k16 step adds 16 of them to the accumulator with an error
+// of at most ~17 * 2^-23 of (sum of |terms| + |accumulator|), so over
+// dpad/16 <= 8 steps G_ij is off by at most ~2^-15.7 sum |a_k b_k| <=
+// 2^-16.7 (|a|^2 + |b|^2), and d~ by at most ~2^-14.7 (G_ii + G_jj).  The
+// reference's fp32 tile-order sum is within ~(dpad/4 + 2) 2^-24 of the sum
+// of its terms (<= 2 (|a|^2 + |b|^2)), i.e. below 2^-17 (G_ii + G_jj).  The
+// total stays under 2^-14.4 (G_ii + G_jj), a 10x margin below eps.
+// ---------------------------------------------------------------------------
+constexpr int kGramMax = 96;             // candidates per target on this path
+constexpr int kGramBrow = kGramMax + 8;  // floats per row of the block-row buffer
+
+__host__ __device__ inline uint32_t gram_k(uint32_t dpad) { return (dpad + 15u) & ~15u; }
+__host__ __device__ inline uint32_t gram_stride(uint32_t dpad) { return gram_k(dpad) * 2u + 16u; }
+__host__ __device__ inline size_t gram_warp_bytes(uint32_t dpad) {
+  const size_t b = size_t(kGramMax) * gram_stride(dpad) + size_t(16) * kGramBrow * 4 +
+                   kGramMax * 4 + 64 * 4;
+  return (b + 15) & ~size_t(15);
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t sa = uint32_t(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem) {
+  const uint32_t sa = uint32_t(__cvta_generic_to_shared(smem));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(sa));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// d(a, b) in the prune's own order, computed by the calling 4-lane tile:
+// L2 over chunks 0 .. dim/8 - 1 (lane s: chunks s, s+4, ...), IP over all
+// dpad/8 chunks (lane s: elements 8c + s, 8c + 4 + s), both reduced xor 2
+// then xor 1 -- RowReg::dist / dist_local with a as the candidate row.
+template <int METRIC>
+__device__ __forceinline__ float exact_pair_dist(const GraphView& g, uint32_t a, uint32_t b,
+                                                 int lane) {
+  const int s = lane & 3;
+  const uint4* ra = reinterpret_cast<const uint4*>(g.vec + size_t(a - g.global_offset) * g.dpad);
+  const uint4* rb = reinterpret_cast<const uint4*>(g.vec + size_t(b - g.global_offset) * g.dpad);
+  float acc = 0.f;
+  if constexpr (METRIC == kL2) {
+    const int nchunks = int(g.dim / 8);
+    for (int c = s; c < nchunks; c += 4) acc = l2_chunk(ldg16(ra + c), ldg16(rb + c), acc);
+    return tile4_sum_local(acc, lane);
+  } else {
+    const uint32_t* a32 = reinterpret_cast<const uint32_t*>(ra);
+    const uint32_t* b32 = reinterpret_cast<const uint32_t*>(rb);
+    const int w = s >> 1;
+    const int nck = int(g.dpad / 8);
+    for (int c = 0; c < nck; c++)
+      acc = ip_pair(__ldg(a32 + 4 * c + w), __ldg(a32 + 4 * c + 2 + w), __ldg(b32 + 4 * c + w),
+                    __ldg(b32 + 4 * c + 2 + w), s, acc);
+    return -tile4_sum_local(acc, lane);
+  }
+}
+
+// RobustPrune of sorted cand[0, nc) (nc <= kGramMax) through the Gram
+// filter; writes the row of `self` like prune_and_write.
+template <int METRIC>
+__device__ void gram_prune_and_write(const GraphView& g, uint32_t self, PruneSmem& sm,
+                                     char* gbase, int nc, float alpha, int lane) {
+  const uint32_t R = g.R;
+  const int K = int(gram_k(g.dpad));
+  const int stride = int(gram_stride(g.dpad));
+  const int nuse = METRIC == kL2 ? int(g.dim / 8) : int(g.dpad / 8);
+  char* rows = gbase;
+  float* brow = reinterpret_cast<float*>(gbase + size_t(kGramMax) * stride);
+  float* norm = brow + 16 * kGramBrow;
+  uint32_t* kpos = reinterpret_cast<uint32_t*>(norm + kGramMax);
+  // Stage the rows: lane -> chunk (lane & 15) of row r0 + (lane >> 4).
+  {
+    const int kc = K / 8;
+    const int c = lane & 15;
+    for (int r = lane >> 4; r < nc; r += 2) {
+      if (c >= kc) continue;
+      char* dst = rows + size_t(r) * stride + c * 16;
+      if (c < nuse) {
+        const uint32_t id = pair_id(sm.cand[r]);
+        cp_async16(dst, g.vec + size_t(id - g.global_offset) * g.dpad + c * 8);
+      } else {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    cp_async_wait_all();
+    __syncwarp();
+  }
+  const int gq = lane >> 2, tq = lane & 3;
+  const int nb = (nc + 15) >> 4;
+  const int nks = K / 16;
+  uint32_t ns = 0;
+  // ldmatrix row addresses: A rows (lane & 15), k half (lane >> 4);
+  // B rows (lane & 7) + 8 (lane >> 4), k half ((lane >> 3) & 1).
+  const int a_row = lane & 15, a_k = (lane >> 4) * 8;
+  const int b_row = (lane & 7) + ((lane >> 4) << 3), b_k = ((lane >> 3) & 1) * 8;
+  for (int I = 0; I < nb && ns < R; I++) {
+    uint32_t af[8][4];
+#pragma unroll
+    for (int kk = 0; kk < 8; kk++)
+      if (kk < nks) ldsm_x4(af[kk], rows + size_t(16 * I + a_row) * stride + (16 * kk + a_k) * 2);
+    for (int J = 0; J <= I; J++) {
+      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kk = 0; kk < 8; kk++) {
+        if (kk < nks) {
+          uint32_t bf[4];
+          ldsm_x4(bf, rows + size_t(16 * J + b_row) * stride + (16 * kk + b_k) * 2);
+          mma16816(c0, af[kk], bf[0], bf[1]);
+          mma16816(c1, af[kk], bf[2], bf[3]);
+        }
+      }
+      float* r0 = brow + gq * kGramBrow + 16 * J + 2 * tq;
+      float* r1 = r0 + 8 * kGramBrow;
+      *reinterpret_cast<float2*>(r0) = make_float2(c0[0], c0[1]);
+      *reinterpret_cast<float2*>(r1) = make_float2(c0[2], c0[3]);
+      *reinterpret_cast<float2*>(r0 + 8) = make_float2(c1[0], c1[1]);
+      *reinterpret_cast<float2*>(r1 + 8) = make_float2(c1[2], c1[3]);
+    }
+    __syncwarp();
+    if (lane < 16) norm[16 * I + lane] = brow[lane * kGramBrow + 16 * I + lane];
+    __syncwarp();
+    const int iend = min(nc, 16 * I + 16);
+    for (int i = 16 * I; i < iend && ns < R; i++) {
+      const uint64_t key = sm.cand[i];
+      const uint32_t cid = pair_id(key);
+      if (cid == self || cid == kInvalid) continue;
+      const float cd = key_dist(key);
+      const float* gr = brow + (i - 16 * I) * kGramBrow;
+      const float ni = norm[i];
+      bool pr = false;
+      uint32_t amb = 0;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const uint32_t m = uint32_t(lane + 32 * h);
+        if (m < ns) {
+          const int j = int(kpos[m]);
+          const float nj = norm[j];
+          const float gij = gr[j];
+          const float approx = METRIC == kL2 ? __fsub_rn(__fadd_rn(ni, nj), __fmul_rn(2.f, gij)) : -gij;
+          const float eps = __fmul_rn(__fadd_rn(ni, nj), 0x1p-11f);
+          if (__fmul_rn(__fadd_rn(approx, eps), alpha) < cd) pr = true;
+          else if (!(__fmul_rn(__fsub_rn(approx, eps), alpha) >= cd)) amb |= 1u << h;
+        }
+      }
+      bool pruned = __any_sync(kFull, pr);
+      if (!pruned) {
+        uint64_t am = uint64_t(__ballot_sync(kFull, amb & 1u)) |
+                      (uint64_t(__ballot_sync(kFull, (amb >> 1) & 1u)) << 32);
+        while (am != 0 && !pruned) {
+          // tile t takes the t-th ambiguous kept row of this pass
+          uint64_t rem = am;
+          const int tile = lane >> 2;
+          for (int t = 0; t < tile && rem; t++) rem &= rem - 1;
+          bool p = false;
+          if (rem != 0) {
+            const int m = __ffsll(static_cast<long long>(rem)) - 1;
+            const float d = exact_pair_dist<METRIC>(g, cid, sm.sel[m], lane);
+            p = __fmul_rn(d, alpha) < cd;
+          }
+          pruned = __any_sync(kFull, p);
+          for (int t = 0; t < 8 && am; t++) am &= am - 1;
+        }
+      }
+      if (!pruned) {
+        if (lane == 0) {
+          sm.sel[ns] = cid;
+          sm.sel_d[ns] = cd;
+          kpos[ns] = uint32_t(i);
+        }
+        ns++;
+        __syncwarp();
+      }
+    }
+    __syncwarp();
+  }
+  const uint32_t l = self - g.global_offset;
+  for (uint32_t i = lane; i < ns; i += 32) {
+    g.edges[size_t(l) * R + i] = sm.sel[i];
+    g.edist[size_t(l) * R + i] = float_to_bf16_bits(sm.sel_d[i]);
+  }
+  if (lane == 0) g.counts[l] = uint8_t(ns);
+  __syncwarp();
+}
+
 // (b) + (c) for batch rows [off, off + bs).
 template <int MAXC, int METRIC>
 __global__ void __launch_bounds__(128) batch_prune_kernel(GraphView g, uint32_t off, uint32_t bs,
@@ -416,14 +630,17 @@ __global__ void group_starts_kernel(const uint64_t* keys, size_t total, uint32_t
 }
 
 // (e) one warp per reverse-edge target.
-template <int MAXC, int METRIC>
+template <int MAXC, int METRIC, bool GRAM>
 __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const uint64_t* keys,
                                                             size_t total, const uint32_t* starts,
                                                             const uint32_t* n_groups, float alpha) {
   extern __shared__ __align__(16) char smem_raw[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int tile = lane >> 2, s = lane & 3;
-  PruneSmem sm = prune_carve(smem_raw + prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) * wid, g.dpad);
+  const size_t wbytes = prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on);
+  const size_t gbytes = GRAM ? gram_warp_bytes(g.dpad) : 0;
+  char* wbase = smem_raw + (wbytes + gbytes) * wid;
+  PruneSmem sm = prune_carve(wbase, g.dpad);
   const uint32_t R = g.R;
   const uint32_t cap = 256 + R;  // MAX_CANDS of construct.cuh:574
   const uint32_t ng = *n_groups;
@@ -489,7 +706,8 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
 #ifdef JB_BUILD_CLOCKS
     long long _c2 = clock64();
 #endif
-    prune_and_write<MAXC, METRIC>(g, t, sm, nc, alpha, lane);
+    if (GRAM && nc <= kGramMax) gram_prune_and_write<METRIC>(g, t, sm, wbase + wbytes, nc, alpha, lane);
+    else prune_and_write<MAXC, METRIC>(g, t, sm, nc, alpha, lane);
 #ifdef JB_BUILD_CLOCKS
     long long _c3 = clock64();
     if (lane == 0) {
@@ -500,6 +718,17 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
     }
 #endif
   }
+}
+
+// The Gram filter takes the same prune decisions as the plain loop; the
+// environment variable JB_GRAM_PRUNE=0 selects the plain loop (for timing
+// comparisons).
+bool gram_prune_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("JB_GRAM_PRUNE");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
 }
 
 template <int MAXC, int METRIC>
@@ -513,22 +742,32 @@ struct Kernels {
     k<<<blocks, 128, smem, st>>>(g, off, bs, ws.vis_idx, ws.vis_dist, ws.vis_cnt, kBuildMaxResult,
                                  alpha);
   }
-  static void reverse(const GraphView& g, size_t total, const BuildWorkspace& ws, float alpha,
-                      cudaStream_t st) {
-    const size_t smem = prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) * 4;
-    auto k = reverse_prune_kernel<MAXC, METRIC>;
+  template <bool GRAM>
+  static void reverse_launch(const GraphView& g, size_t total, const BuildWorkspace& ws,
+                             float alpha, cudaStream_t st) {
+    const int warps = GRAM ? 2 : 4;
+    const size_t smem = (prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) +
+                         (GRAM ? gram_warp_bytes(g.dpad) : 0)) * warps;
+    auto k = reverse_prune_kernel<MAXC, METRIC, GRAM>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     int dev = 0, sms = 0, per_sm = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 128, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 32 * warps, smem);
     if (per_sm < 1) per_sm = 1;
     size_t blocks = size_t(sms) * per_sm;
-    const size_t need = (total + 3) / 4;
+    const size_t need = (total + warps - 1) / warps;
     if (blocks > need) blocks = need;
     if (blocks == 0) blocks = 1;
-    k<<<uint32_t(blocks), 128, smem, st>>>(g, ws.rev_sorted, total, ws.group_starts,
-                                           ws.counters + 1, alpha);
+    k<<<uint32_t(blocks), 32 * warps, smem, st>>>(g, ws.rev_sorted, total, ws.group_starts,
+                                                  ws.counters + 1, alpha);
+  }
+  static void reverse(const GraphView& g, size_t total, const BuildWorkspace& ws, float alpha,
+                      cudaStream_t st) {
+    if (gram_prune_enabled() && g.dpad <= 128 && alpha > 0.f)
+      reverse_launch<true>(g, total, ws, alpha, st);
+    else
+      reverse_launch<false>(g, total, ws, alpha, st);
   }
 };
 

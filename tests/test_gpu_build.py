@@ -28,7 +28,23 @@ CASES = [
     ("relu_sphere", 1500, 320, 32, 1, 1.0),
     # batches of 400 rows: hub targets collect more than 256 + R candidates
     ("sift_like", 20000, 128, 64, 0, 1.2),
+    # exact duplicate rows (zero pair distances) and near ties on the prune
+    # threshold: exercises the exact fallback of the Gram-filtered prune
+    ("dup_sift", 4000, 128, 32, 0, 1.2),
+    ("dup_sift", 3000, 64, 16, 1, 1.0),
 ]
+
+
+def dup_sift(n, dim, seed):
+    """sift_like rows, each repeated four times (some with one coordinate
+    nudged by one step), in shuffled order."""
+    base = synthetic.sift_like((n + 3) // 4, dim, seed)
+    X = np.repeat(base, 4, axis=0)[:n].copy()
+    rng = np.random.default_rng(seed)
+    nudge = rng.random(n) < 0.3
+    cols = rng.integers(0, dim, size=n)
+    X[nudge, cols[nudge]] += np.float16(1.0)
+    return X[rng.permutation(n)]
 
 
 def assert_graph_equal(e, d, c, g, msg=""):
@@ -42,7 +58,7 @@ def assert_graph_equal(e, d, c, g, msg=""):
 @pytest.mark.parametrize("case", CASES, ids=lambda c: f"{c[0]}-n{c[1]}-d{c[2]}-R{c[3]}-m{c[4]}")
 def test_build_matches_oracle(cuda, case):
     kind, n, dim, R, metric, alpha = case
-    X = getattr(synthetic, kind)(n, dim, 31)
+    X = dup_sift(n, dim, 31) if kind == "dup_sift" else getattr(synthetic, kind)(n, dim, 31)
     budget = 10 * 10**9
     g = O.OracleGraph(X, R, metric=metric)
     g.build(alpha, max(1, O.reference_max_batch_size(budget, n, R)))
