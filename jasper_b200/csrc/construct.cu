@@ -232,6 +232,52 @@ __device__ __forceinline__ void sort_cands(uint64_t* cand, int nc, int lane) {
   warp_sort_smem(cand, n, lane);
 }
 
+// Sort cand[0, nc) where cand[0, na) are a target's existing edges and
+// cand[na, nc) its new sinks.  The existing edges were written in candidate
+// order with bf16-rounded distances, so they are usually sorted already
+// (rounding is monotone; only ids inside a bf16 tie can be out of order).
+// When they are and the sinks fit in one warp, the sinks are ranked in
+// registers and both lists are merged in place by rank; otherwise the full
+// bitonic sort runs.  Equal keys are identical values, so both give the same
+// array.
+__device__ __forceinline__ void sort_cands_merge(uint64_t* cand, int na, int nc, int lane) {
+  const int nb = nc - na;
+  bool fast = na <= 64 && nb <= 32;
+  if (fast) {
+    bool bad = false;
+    for (int i = lane; i + 1 < na; i += 32) bad |= cand[i] > cand[i + 1];
+    fast = !__any_sync(kFull, bad);
+  }
+  if (!fast) {
+    sort_cands(cand, nc, lane);
+    return;
+  }
+  const uint64_t b = lane < nb ? cand[na + lane] : kKeyMax;
+  const uint64_t a0 = lane < na ? cand[lane] : kKeyMax;
+  const uint64_t a1 = lane + 32 < na ? cand[lane + 32] : kKeyMax;
+  int rb = 0, c0 = 0, c1 = 0;
+  for (int t = 0; t < nb; t++) {
+    const uint64_t o = __shfl_sync(kFull, b, t);
+    rb += (o < b || (o == b && t < lane)) ? 1 : 0;
+    c0 += o < a0 ? 1 : 0;
+    c1 += o < a1 ? 1 : 0;
+  }
+  int ca = 0;  // existing edges <= b
+  if (lane < nb) {
+    int lo = 0, hi = na;
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (cand[mid] <= b) lo = mid + 1; else hi = mid;
+    }
+    ca = lo;
+  }
+  __syncwarp();
+  if (lane < na) cand[lane + c0] = a0;
+  if (lane + 32 < na) cand[lane + 32 + c1] = a1;
+  if (lane < nb) cand[rb + ca] = b;
+  __syncwarp();
+}
+
 // RobustPrune over sorted candidate pair keys; writes the row of `self`.
 template <int MAXC, int METRIC>
 __device__ void prune_and_write(const GraphView& gv, uint32_t self, PruneSmem& sm, int nc,
@@ -375,7 +421,13 @@ __device__ void prune_and_write(const GraphView& gv, uint32_t self, PruneSmem& s
 // of its terms (<= 2 (|a|^2 + |b|^2)), i.e. below 2^-17 (G_ii + G_jj).  The
 // total stays under 2^-14.4 (G_ii + G_jj), a 10x margin below eps.
 // ---------------------------------------------------------------------------
-constexpr int kGramMax = 96;             // candidates per target on this path
+#ifndef JB_GRAM_MAX
+#define JB_GRAM_MAX 96
+#endif
+#ifndef JB_GRAM_WARPS
+#define JB_GRAM_WARPS 2
+#endif
+constexpr int kGramMax = JB_GRAM_MAX;    // candidates per target on this path
 constexpr int kGramBrow = kGramMax + 8;  // floats per row of the block-row buffer
 
 __host__ __device__ inline uint32_t gram_k(uint32_t dpad) { return (dpad + 15u) & ~15u; }
@@ -664,6 +716,7 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
 #ifdef JB_BUILD_CLOCKS
     long long _c0 = clock64();
 #endif
+    const int na = nc;
     RowReg<MAXC, METRIC> tr;
     tr.load(g, t, nchunks, lane, sm.row);
     // The group is the contiguous run of keys with this target.
@@ -702,7 +755,7 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
 #ifdef JB_BUILD_CLOCKS
     long long _c1 = clock64();
 #endif
-    sort_cands(sm.cand, nc, lane);
+    sort_cands_merge(sm.cand, na, nc, lane);
 #ifdef JB_BUILD_CLOCKS
     long long _c2 = clock64();
 #endif
@@ -745,7 +798,7 @@ struct Kernels {
   template <bool GRAM>
   static void reverse_launch(const GraphView& g, size_t total, const BuildWorkspace& ws,
                              float alpha, cudaStream_t st) {
-    const int warps = GRAM ? 2 : 4;
+    const int warps = GRAM ? JB_GRAM_WARPS : 4;
     const size_t smem = (prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) +
                          (GRAM ? gram_warp_bytes(g.dpad) : 0)) * warps;
     auto k = reverse_prune_kernel<MAXC, METRIC, GRAM>;
