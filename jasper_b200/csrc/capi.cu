@@ -11,6 +11,7 @@
 #include <tuple>
 #include <map>
 #include <mutex>
+#include <set>
 #include <stdexcept>
 #include <string>
 #include <unordered_map>
@@ -111,12 +112,36 @@ void check_metric(int32_t metric) {
 // the padded dim are first packed into a padded scratch copy.
 // rq_margin >= 0 turns on the RaBitQ candidate filter; `rotate` applies the
 // graph's prerotation to the queries first.
+// The device's default stream-ordered pool returns all freed memory to the
+// driver at every synchronisation (release threshold 0), so a search's
+// per-call buffers (queries, results, work counter) would be mapped afresh on
+// every call.  Keep up to 256 MiB reserved in the pool between calls, once per
+// device; larger transient buffers (the build's) are still released.
+void retain_small_pool_memory() {
+  static std::mutex m;
+  static std::set<int> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return; }
+  std::lock_guard<std::mutex> lock(m);
+  if (!done.insert(dev).second) return;
+  cudaMemPool_t pool;
+  if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+    uint64_t keep = uint64_t(256) << 20;
+    uint64_t cur = 0;
+    if (cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &cur) == cudaSuccess &&
+        cur < keep)
+      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
+  cudaGetLastError();
+}
+
 void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint32_t row_stride,
                  int32_t* out_idx, float* out_dist, uint32_t k, uint32_t bw, uint32_t limit,
                  uint32_t* stats, uint32_t* seen, cudaStream_t st, float rq_margin = -1.0f,
                  bool rotate = false) {
   if (nq == 0) return;
   if (nq > 0x7FFFFFFFull) throw std::invalid_argument("too many queries");
+  retain_small_pool_memory();
   if (k == 0) throw std::invalid_argument("k must be > 0");
   if (row_stride < g.dim) throw std::invalid_argument("row_stride < dim");
   if (out_idx == nullptr || out_dist == nullptr || queries == nullptr)
