@@ -409,17 +409,17 @@ __device__ void prune_and_write(const GraphView& gv, uint32_t self, PruneSmem& s
 //     fl((d~ + eps) * alpha) <  cd  =>  pruned,
 //     fl((d~ - eps) * alpha) >= cd  =>  not pruned by j,
 // and only pairs inside the band are evaluated exactly, in the reference's
-// order (exact_pair_dist).  The decisions, and so the kept list, are the
+// order from the staged rows (exact_pair_smem).  The decisions, and so the kept list, are the
 // ones prune_and_write takes.
 //
-// eps = 2^-11 (G_ii + G_jj).  Error budget: the fp16 products are exact in
+// eps = 2^-12 (G_ii + G_jj).  Error budget: the fp16 products are exact in
 // fp32; one m16n8k16 step adds 16 of them to the accumulator with an error
 // of at most ~17 * 2^-23 of (sum of |terms| + |accumulator|), so over
 // dpad/16 <= 8 steps G_ij is off by at most ~2^-15.7 sum |a_k b_k| <=
 // 2^-16.7 (|a|^2 + |b|^2), and d~ by at most ~2^-14.7 (G_ii + G_jj).  The
 // reference's fp32 tile-order sum is within ~(dpad/4 + 2) 2^-24 of the sum
 // of its terms (<= 2 (|a|^2 + |b|^2)), i.e. below 2^-17 (G_ii + G_jj).  The
-// total stays under 2^-14.4 (G_ii + G_jj), a 10x margin below eps.
+// total stays under 2^-14.4 (G_ii + G_jj), a 5x margin below eps.
 // ---------------------------------------------------------------------------
 #ifndef JB_GRAM_MAX
 #define JB_GRAM_MAX 96
@@ -428,6 +428,10 @@ __device__ void prune_and_write(const GraphView& gv, uint32_t self, PruneSmem& s
 #define JB_GRAM_WARPS 2
 #endif
 constexpr int kGramMax = JB_GRAM_MAX;    // candidates per target on this path
+#ifndef JB_GRAM_EPS_LOG2
+#define JB_GRAM_EPS_LOG2 12
+#endif
+constexpr float kGramEps = 1.0f / float(1 << JB_GRAM_EPS_LOG2);
 constexpr int kGramBrow = kGramMax + 8;  // floats per row of the block-row buffer
 
 __host__ __device__ inline uint32_t gram_k(uint32_t dpad) { return (dpad + 15u) & ~15u; }
@@ -459,29 +463,28 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// d(a, b) in the prune's own order, computed by the calling 4-lane tile:
-// L2 over chunks 0 .. dim/8 - 1 (lane s: chunks s, s+4, ...), IP over all
-// dpad/8 chunks (lane s: elements 8c + s, 8c + 4 + s), both reduced xor 2
-// then xor 1 -- RowReg::dist / dist_local with a as the candidate row.
+// d(i, j) of two staged rows in the prune's own order, computed by the
+// calling 4-lane tile: L2 over chunks 0 .. dim/8 - 1 (lane s: chunks s,
+// s+4, ...), IP over all dpad/8 chunks (lane s: elements 8c + s, 8c + 4 + s),
+// both reduced xor 2 then xor 1 -- RowReg::dist / dist_local with row i as
+// the candidate.  nck is the number of staged chunks (dim/8 for L2, dpad/8
+// for IP); the staged chunks are the rows' own bytes.
 template <int METRIC>
-__device__ __forceinline__ float exact_pair_dist(const GraphView& g, uint32_t a, uint32_t b,
-                                                 int lane) {
+__device__ __forceinline__ float exact_pair_smem(const char* rows, int stride, int i, int j,
+                                                 int nck, int lane) {
   const int s = lane & 3;
-  const uint4* ra = reinterpret_cast<const uint4*>(g.vec + size_t(a - g.global_offset) * g.dpad);
-  const uint4* rb = reinterpret_cast<const uint4*>(g.vec + size_t(b - g.global_offset) * g.dpad);
+  const uint4* ra = reinterpret_cast<const uint4*>(rows + size_t(i) * stride);
+  const uint4* rb = reinterpret_cast<const uint4*>(rows + size_t(j) * stride);
   float acc = 0.f;
   if constexpr (METRIC == kL2) {
-    const int nchunks = int(g.dim / 8);
-    for (int c = s; c < nchunks; c += 4) acc = l2_chunk(ldg16(ra + c), ldg16(rb + c), acc);
+    for (int c = s; c < nck; c += 4) acc = l2_chunk(ra[c], rb[c], acc);
     return tile4_sum_local(acc, lane);
   } else {
     const uint32_t* a32 = reinterpret_cast<const uint32_t*>(ra);
     const uint32_t* b32 = reinterpret_cast<const uint32_t*>(rb);
     const int w = s >> 1;
-    const int nck = int(g.dpad / 8);
     for (int c = 0; c < nck; c++)
-      acc = ip_pair(__ldg(a32 + 4 * c + w), __ldg(a32 + 4 * c + 2 + w), __ldg(b32 + 4 * c + w),
-                    __ldg(b32 + 4 * c + 2 + w), s, acc);
+      acc = ip_pair(a32[4 * c + w], a32[4 * c + 2 + w], b32[4 * c + w], b32[4 * c + 2 + w], s, acc);
     return -tile4_sum_local(acc, lane);
   }
 }
@@ -568,7 +571,7 @@ __device__ void gram_prune_and_write(const GraphView& g, uint32_t self, PruneSme
           const float nj = norm[j];
           const float gij = gr[j];
           const float approx = METRIC == kL2 ? __fsub_rn(__fadd_rn(ni, nj), __fmul_rn(2.f, gij)) : -gij;
-          const float eps = __fmul_rn(__fadd_rn(ni, nj), 0x1p-11f);
+          const float eps = __fmul_rn(__fadd_rn(ni, nj), kGramEps);
           if (__fmul_rn(__fadd_rn(approx, eps), alpha) < cd) pr = true;
           else if (!(__fmul_rn(__fsub_rn(approx, eps), alpha) >= cd)) amb |= 1u << h;
         }
@@ -585,7 +588,7 @@ __device__ void gram_prune_and_write(const GraphView& g, uint32_t self, PruneSme
           bool p = false;
           if (rem != 0) {
             const int m = __ffsll(static_cast<long long>(rem)) - 1;
-            const float d = exact_pair_dist<METRIC>(g, cid, sm.sel[m], lane);
+            const float d = exact_pair_smem<METRIC>(rows, stride, i, int(kpos[m]), nuse, lane);
             p = __fmul_rn(d, alpha) < cd;
           }
           pruned = __any_sync(kFull, p);
