@@ -527,6 +527,9 @@ __device__ void gram_prune_and_write(const GraphView& g, uint32_t self, PruneSme
   // B rows (lane & 7) + 8 (lane >> 4), k half ((lane >> 3) & 1).
   const int a_row = lane & 15, a_k = (lane >> 4) * 8;
   const int b_row = (lane & 7) + ((lane >> 4) << 3), b_k = ((lane >> 3) & 1) * 8;
+  // This lane's kept slots lane and lane + 32: candidate position and norm.
+  int kj[2] = {0, 0};
+  float knorm[2] = {0.f, 0.f};
   for (int I = 0; I < nb && ns < R; I++) {
     uint32_t af[8][4];
 #pragma unroll
@@ -567,8 +570,8 @@ __device__ void gram_prune_and_write(const GraphView& g, uint32_t self, PruneSme
       for (int h = 0; h < 2; h++) {
         const uint32_t m = uint32_t(lane + 32 * h);
         if (m < ns) {
-          const int j = int(kpos[m]);
-          const float nj = norm[j];
+          const int j = kj[h];
+          const float nj = knorm[h];
           const float gij = gr[j];
           const float approx = METRIC == kL2 ? __fsub_rn(__fadd_rn(ni, nj), __fmul_rn(2.f, gij)) : -gij;
           const float eps = __fmul_rn(__fadd_rn(ni, nj), kGramEps);
@@ -600,6 +603,11 @@ __device__ void gram_prune_and_write(const GraphView& g, uint32_t self, PruneSme
           sm.sel[ns] = cid;
           sm.sel_d[ns] = cd;
           kpos[ns] = uint32_t(i);
+        }
+        // kept slot ns lives in lane ns % 32, register ns / 32
+        if (lane == int(ns & 31u)) {
+          if (ns < 32) { kj[0] = i; knorm[0] = ni; }
+          else { kj[1] = i; knorm[1] = ni; }
         }
         ns++;
         __syncwarp();
