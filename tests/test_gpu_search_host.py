@@ -53,3 +53,28 @@ def test_search_host_matches_device_search(cuda, metric):
             T.assert_same_results(gi, gd, ri, rd, msg=f"padded bw={bw}")
     finally:
         T.free(h)
+
+
+def test_search_host_large_batch(cuda):
+    """A batch larger than the device's resident warps (9001 queries): the
+    results equal the device search, call after call, with the outputs
+    refilled in between."""
+    n, dim, k, bw = 3000, 64, 10, 32
+    X = synthetic.gaussian(n, dim, 71)
+    Q = synthetic.gaussian(9001, dim, 72)
+    h = T.construct(X, 16, 0, 1.2)
+    try:
+        ri, rd = T.search(h, Q, k, bw)
+        qp = torch.from_numpy(O.pad_rows(Q))
+        for q, pinned in ((qp.pin_memory(), True), (qp.clone(), False)):
+            oi = torch.empty(Q.shape[0], k, dtype=torch.int32)
+            od = torch.empty(Q.shape[0], k, dtype=torch.float32)
+            if pinned:
+                oi, od = oi.pin_memory(), od.pin_memory()
+            for _ in range(3):
+                oi.fill_(7)
+                od.fill_(7.0)
+                gi, gd = _host_search(h, q, k, bw, oi, od)
+                T.assert_same_results(gi, gd, ri, rd, msg=f"pinned={pinned}")
+    finally:
+        T.free(h)
