@@ -174,12 +174,15 @@ __device__ __forceinline__ float dist_smemq(const uint16_t* qs, const uint4* row
   return METRIC == kL2 ? acc : -acc;
 }
 
+#ifndef JB_SMEMQ2_BATCH
+#define JB_SMEMQ2_BATCH 8
+#endif
 // Two rows per tile in one loop (independent chains interleaved), each row
 // summed exactly as dist_smemq sums it.
 template <int METRIC>
 __device__ __forceinline__ float2 dist_smemq2(const uint16_t* qs, const uint4* row0, bool a0,
                                               const uint4* row1, bool a1, int nchunks, int s) {
-  constexpr int B = 4;
+  constexpr int B = JB_SMEMQ2_BATCH;  // 16-byte chunks per row in flight per lane
   float acc0 = 0.f, acc1 = 0.f;
   if (METRIC == kL2) {
     const uint4* q4 = reinterpret_cast<const uint4*>(qs);
