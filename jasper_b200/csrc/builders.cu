@@ -103,9 +103,10 @@ __global__ void lsh_edges_kernel(GraphView g, uint32_t k_ranks, uint32_t packed_
   const __half* vec = reinterpret_cast<const __half*>(g.vec);
   for (uint32_t l = blockIdx.x * (blockDim.x >> 5) + wid; l < g.n; l += nw) {
     const __half* u = vec + size_t(l) * g.dpad;
-    const uint32_t cnt = g.counts[l];
+    const uint32_t cnt = min(uint32_t(g.counts[l]), g.R);
     for (uint32_t e = 0; e < cnt; e++) {
       const uint32_t nb = g.edges[size_t(l) * g.R + e];
+      if (nb - g.global_offset >= g.n) continue;  // not a row of this graph: no sketch
       const __half* v = vec + size_t(nb - g.global_offset) * g.dpad;
       const float m2 = delta_keys(u, v, g.dpad, coord_bits, coord_bits + 1, keys, lane);
       for (uint32_t r = 0; r < k_ranks; r++) {
@@ -141,7 +142,7 @@ __global__ void lsh_sample_kernel(GraphView g, uint32_t k_ranks, uint32_t n_samp
         if (cnt == 0) continue;
         const uint32_t e = curand(&rng) % cnt;
         const uint32_t nb = g.edges[size_t(ql) * g.R + e];
-        if (nb == kInvalid) continue;
+        if (nb == kInvalid || nb - g.global_offset >= g.n) continue;
         qg = ql + g.global_offset;
         ng = nb;
         break;
@@ -195,7 +196,7 @@ __global__ void pq_sample_kernel(GraphView g, __half* X, uint32_t n_train, uint6
         if (cnt == 0) continue;
         const uint32_t e = curand(&rng) % cnt;
         const uint32_t nb = g.edges[size_t(q) * g.R + e];
-        if (nb == kInvalid) continue;
+        if (nb == kInvalid || nb - g.global_offset >= g.n) continue;
         ql = q;
         nl = nb - g.global_offset;
         break;
@@ -321,9 +322,10 @@ __global__ void pq_codes_kernel(GraphView g, uint32_t M, const float* C, uint8_t
   const __half* vec = reinterpret_cast<const __half*>(g.vec);
   for (uint32_t l = blockIdx.x * (blockDim.x >> 5) + wid; l < g.n; l += nw) {
     const __half* u = vec + size_t(l) * g.dpad;
-    const uint32_t cnt = g.counts[l];
+    const uint32_t cnt = min(uint32_t(g.counts[l]), g.R);
     for (uint32_t e = 0; e < cnt; e++) {
       const uint32_t nb = g.edges[size_t(l) * g.R + e];
+      if (nb - g.global_offset >= g.n) continue;  // not a row of this graph: no sketch
       const __half* v = vec + size_t(nb - g.global_offset) * g.dpad;
       for (uint32_t i = lane; i < g.dpad; i += 32) res[i] = __half2float(__hsub(v[i], u[i]));
       __syncwarp();

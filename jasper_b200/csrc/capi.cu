@@ -112,27 +112,35 @@ void check_metric(int32_t metric) {
 // the padded dim are first packed into a padded scratch copy.
 // rq_margin >= 0 turns on the RaBitQ candidate filter; `rotate` applies the
 // graph's prerotation to the queries first.
-// The device's default stream-ordered pool returns all freed memory to the
-// driver at every synchronisation (release threshold 0), so a search's
-// per-call buffers (queries, results, work counter) would be mapped afresh on
-// every call.  Keep up to 256 MiB reserved in the pool between calls, once per
-// device; larger transient buffers (the build's) are still released.
-void retain_small_pool_memory() {
+// Per-call search buffers (repacked queries, results, work counter) come from
+// a stream-ordered pool of the library's own, one per device, that keeps up to
+// 256 MiB reserved between calls: a pool with the default release threshold of
+// 0 hands its memory back to the driver at every synchronisation, so each call
+// would map it afresh.  The device's default pool, which other libraries in
+// the process share, is left as it is.
+cudaMemPool_t search_pool() {
   static std::mutex m;
-  static std::set<int> done;
+  static std::map<int, cudaMemPool_t> pools;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) { cudaGetLastError(); return; }
+  cuda_check(cudaGetDevice(&dev), "get device");
   std::lock_guard<std::mutex> lock(m);
-  if (!done.insert(dev).second) return;
+  auto it = pools.find(dev);
+  if (it != pools.end()) return it->second;
+  cudaMemPoolProps props{};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = dev;
   cudaMemPool_t pool;
-  if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
-    uint64_t keep = uint64_t(256) << 20;
-    uint64_t cur = 0;
-    if (cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &cur) == cudaSuccess &&
-        cur < keep)
-      cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
-  }
-  cudaGetLastError();
+  cuda_check(cudaMemPoolCreate(&pool, &props), "create search pool");
+  uint64_t keep = uint64_t(256) << 20;
+  cuda_check(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep),
+             "set search pool threshold");
+  pools[dev] = pool;
+  return pool;
+}
+
+void pool_alloc(void** p, size_t bytes, cudaStream_t st, const char* what) {
+  cuda_check(cudaMallocFromPoolAsync(p, bytes, search_pool(), st), what);
 }
 
 void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint32_t row_stride,
@@ -141,7 +149,6 @@ void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint3
                  bool rotate = false) {
   if (nq == 0) return;
   if (nq > 0x7FFFFFFFull) throw std::invalid_argument("too many queries");
-  retain_small_pool_memory();
   if (k == 0) throw std::invalid_argument("k must be > 0");
   if (row_stride < g.dim) throw std::invalid_argument("row_stride < dim");
   if (out_idx == nullptr || out_dist == nullptr || queries == nullptr)
@@ -151,7 +158,7 @@ void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint3
   void* counter = nullptr;
   const bool aligned = (reinterpret_cast<uintptr_t>(queries) % 16) == 0;
   if (row_stride != g.dpad || !aligned || rotate) {
-    cuda_check(cudaMallocAsync(&packed, size_t(nq) * g.dpad * 2, st), "alloc packed queries");
+    pool_alloc(reinterpret_cast<void**>(&packed), size_t(nq) * g.dpad * 2, st, "alloc packed queries");
     cuda_check(cudaMemsetAsync(packed, 0, size_t(nq) * g.dpad * 2, st), "clear packed queries");
     cuda_check(cudaMemcpy2DAsync(packed, size_t(g.dpad) * 2, queries, size_t(row_stride) * 2,
                                  size_t(g.dim) * 2, nq, cudaMemcpyDefault, st),
@@ -166,7 +173,7 @@ void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint3
     }
     q = static_cast<const uint16_t*>(packed);
   }
-  cuda_check(cudaMallocAsync(&counter, jb::kSearchScratchBytes, st), "alloc search scratch");
+  pool_alloc(reinterpret_cast<void**>(&counter), jb::kSearchScratchBytes, st, "alloc search scratch");
   cuda_check(cudaMemsetAsync(counter, 0, jb::kSearchScratchBytes, st), "clear search scratch");
   jb::SearchArgs a{};
   a.g = g.view();
@@ -319,10 +326,10 @@ int jb_graph_search_host(int64_t handle, const uint16_t* queries, uint64_t n_que
     const size_t qbytes = size_t(n_queries) * g->dpad * 2;
     const size_t obytes = size_t(n_queries) * k * 4;
     void *dq = nullptr, *di = nullptr, *dd = nullptr;
-    cuda_check(cudaMallocAsync(&dq, qbytes, st), "alloc queries");
-    cuda_check(cudaMallocAsync(&di, obytes, st), "alloc out idx");
-    cuda_check(cudaMallocAsync(&dd, obytes, st), "alloc out dist");
     try {
+      pool_alloc(&dq, qbytes, st, "alloc queries");
+      pool_alloc(&di, obytes, st, "alloc out idx");
+      pool_alloc(&dd, obytes, st, "alloc out dist");
       if (row_stride == g->dpad) {
         cuda_check(cudaMemcpyAsync(dq, queries, qbytes, cudaMemcpyHostToDevice, st), "copy queries");
       } else {
@@ -336,7 +343,8 @@ int jb_graph_search_host(int64_t handle, const uint16_t* queries, uint64_t n_que
       cuda_check(cudaMemcpyAsync(out_idx, di, obytes, cudaMemcpyDeviceToHost, st), "copy idx");
       cuda_check(cudaMemcpyAsync(out_dist, dd, obytes, cudaMemcpyDeviceToHost, st), "copy dist");
     } catch (...) {
-      cudaFreeAsync(dq, st); cudaFreeAsync(di, st); cudaFreeAsync(dd, st);
+      for (void* p : {dq, di, dd})
+        if (p) cudaFreeAsync(p, st);
       cudaStreamSynchronize(st);
       throw;
     }
@@ -578,7 +586,7 @@ int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* qu
     const size_t qbytes = size_t(n_queries) * g->dpad * 2;
     const bool aligned = (reinterpret_cast<uintptr_t>(queries) % 16) == 0;
     if (row_stride != g->dpad || !aligned || d.prerotate) {
-      cuda_check(cudaMallocAsync(&packed, qbytes, st), "alloc queries");
+      pool_alloc(reinterpret_cast<void**>(&packed), qbytes, st, "alloc queries");
       cuda_check(cudaMemsetAsync(packed, 0, qbytes, st), "clear queries");
       cuda_check(cudaMemcpy2DAsync(packed, size_t(g->dpad) * 2, queries, size_t(row_stride) * 2,
                                    size_t(g->dim) * 2, n_queries, cudaMemcpyDefault, st),
@@ -586,7 +594,7 @@ int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* qu
       if (d.prerotate) jb::rotate_rows_inplace(*g, static_cast<uint16_t*>(packed), n_queries, st);
       q = static_cast<const uint16_t*>(packed);
     }
-    cuda_check(cudaMallocAsync(&counter, 256, st), "alloc counter");
+    pool_alloc(reinterpret_cast<void**>(&counter), 256, st, "alloc counter");
     cuda_check(cudaMemsetAsync(counter, 0, 256, st), "clear counter");
     jb::DirSearchArgs a{};
     a.g = g->view();

@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(128) dir_search_kernel(DirSearchArgs a) {
 
       // Neighbours of u with estimated distances.
       const uint32_t lu = u - lo;
-      const uint32_t ne = g.counts[lu];
+      const uint32_t ne = min(uint32_t(g.counts[lu]), R);
       int m = 0;
       for (uint32_t e0 = 0; e0 < ne; e0 += 32) {
         const uint32_t e = e0 + lane;

@@ -149,6 +149,9 @@ void graph_load_file(Graph& g, const std::string& path, uint32_t dim, uint32_t R
                              " does not match dim=" + std::to_string(dim) +
                              " n_neighbors=" + std::to_string(R));
   if (n >= 0x7FFFFFFFull) throw std::runtime_error("graph file has too many rows");
+  if (n > 0 && medoid >= n)
+    throw std::runtime_error("graph file " + path + ": medoid " + std::to_string(medoid) +
+                             " is not a row of the file (n=" + std::to_string(n) + ")");
   graph_allocate(g, dim, R, metric, uint32_t(n), on_host);
   g.medoid = uint32_t(medoid);
   try {
@@ -175,6 +178,20 @@ void graph_load_file(Graph& g, const std::string& path, uint32_t dim, uint32_t R
         p += 1;
         memcpy(&he[i * R], p, 4ull * R);
         p += 4ull * R;
+        // Every kernel walks the first count edges of a row and gathers their
+        // rows, so a count above R or an id outside the file would read past
+        // the arrays: reject the file before anything reaches the device.
+        if (hc[i] > R)
+          throw std::runtime_error("graph file " + path + ": row " + std::to_string(start + i) +
+                                   " has edge count " + std::to_string(hc[i]) + " > n_neighbors " +
+                                   std::to_string(R));
+        for (uint32_t e = 0; e < hc[i]; e++) {
+          const uint32_t id = he[i * R + e];
+          if (id != 0xFFFFFFFFu && id >= n)
+            throw std::runtime_error("graph file " + path + ": row " + std::to_string(start + i) +
+                                     " has neighbour id " + std::to_string(id) + " >= n " +
+                                     std::to_string(n));
+        }
         memcpy(&hd[i * R], p, 2ull * R);
         p += 2ull * R;
         if (inline_del) {

@@ -8,9 +8,9 @@
 #   -rdc=true -lineinfo (CMakeLists.txt:19), JASPER_STABLE_IDS=0 and
 #   JASPER_ENABLE_COMPACT=0 (the shipped defaults, graph.cuh:29-34), no NDEBUG
 #   (device asserts stay on, as in the reference's default build type).
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default /root/reference)
+# Usage: oracle/build_ref.sh REFERENCE_ROOT
 set -euo pipefail
-REF=${1:-/root/reference}
+REF=${1:?usage: oracle/build_ref.sh REFERENCE_ROOT}
 HERE=$(cd "$(dirname "$0")" && pwd)
 OUT=$HERE/_ref
 TVM=$(python -c "import tvm_ffi,os;print(os.path.dirname(tvm_ffi.__file__))")

@@ -8,7 +8,8 @@ Restates the reference's artifact builders deterministically:
   B = 7 (dim ≤ 128, uint8 words) or 15 (uint16 words); k_ranks rounds of
   argmax, each winner stored as its low B+1 bits and then zeroed; edge
   magnitude² = bf16(Σ float(Δ)²).  Only slots below the edge count are
-  filled (the reference walks all R slots).
+  filled (the reference walks all R slots and reads the rows behind the
+  unset ones).
 * LSH globals -- accumulate_rank_sums / finalize_lsh_globals
   (lsh_globals.cuh:17-177): c_r = mean over sampled edges of
   |Δ|_(r) / ‖Δ‖, norm_denom = Σ c_r².  Edges are sampled with numpy here

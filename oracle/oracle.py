@@ -7,6 +7,7 @@ never imports it.  Build with ``make -C oracle`` (or __graft_entry__.build()).
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from pathlib import Path
 
@@ -29,8 +30,8 @@ _lib = None
 
 
 def build() -> Path:
-    src = HERE / "jasper_oracle.c"
-    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+    srcs = [HERE / "jasper_oracle.c", HERE / "bruteforce.c"]
+    if not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < max(s.stat().st_mtime for s in srcs):
         subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
     return LIB_PATH
 
@@ -165,6 +166,28 @@ def bruteforce(base: np.ndarray, queries: np.ndarray, k: int, metric: int = 0):
     od = np.zeros((nq, k), dtype=np.float32)
     lib().orc_bruteforce(_p(b), b.shape[0], _p(q), nq, b.shape[1], metric, k, _p(oi), _p(od))
     return oi.view(np.int32), od
+
+
+def bruteforce_knn(base: np.ndarray, queries: np.ndarray, k: int, metric: int = 0,
+                   threads: int | None = None):
+    """The timed CPU baseline (oracle/bruteforce.c): exact k-NN of fp32
+    rows over fp32 queries on `threads` host threads (default: all), distance
+    ascending then id.  Returns (ids int32 [nq, k], distances float32)."""
+    b = np.ascontiguousarray(base, dtype=np.float32)
+    q = np.ascontiguousarray(queries, dtype=np.float32)
+    assert b.ndim == 2 and q.ndim == 2 and b.shape[1] == q.shape[1]
+    L = lib()
+    L.orc_bruteforce_knn.argtypes = [C.c_void_p, C.c_uint64, C.c_void_p, C.c_uint64, C.c_uint32,
+                                     C.c_uint32, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+    L.orc_bruteforce_knn.restype = C.c_int
+    nq = q.shape[0]
+    oi = np.empty((nq, k), dtype=np.int32)
+    od = np.empty((nq, k), dtype=np.float32)
+    rc = L.orc_bruteforce_knn(_p(b), b.shape[0], _p(q), nq, b.shape[1], k, metric,
+                              int(threads or os.cpu_count() or 1), _p(oi), _p(od))
+    if rc != 0:
+        raise ValueError("orc_bruteforce_knn: bad arguments")
+    return oi, od
 
 
 def reference_max_batch_size(budget_bytes: int, n: int, R: int) -> int:

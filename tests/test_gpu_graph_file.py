@@ -106,3 +106,37 @@ def test_bad_files_raise(cuda, tmp_path):
     p2.write_bytes(struct.pack("<4Q", 0, 10, 0, 12345))
     with pytest.raises(OSError):
         load(p2, 32, 16)
+
+
+def test_corrupt_records_rejected_before_any_kernel(cuda, tmp_path):
+    """A file whose medoid, edge count or neighbour ids point outside the
+    file is rejected by the loader itself: every kernel walks the first
+    count edges of a row and gathers the rows they name."""
+    X = synthetic.gaussian(400, 32, 45)
+    h = T.construct(X, 16, 0, 1.2)
+    try:
+        p = tmp_path / "g.graph"
+        _lib.call("jb_graph_save", h, str(p).encode())
+    finally:
+        T.free(h)
+    raw = bytearray(p.read_bytes())
+    n, dim, R = 400, 32, 16
+    bpn = 2 * dim + 1 + 6 * R + 4
+    T.free(load(p, dim, R))                                # the intact file loads
+    cases = {}
+    bad = bytearray(raw)
+    struct.pack_into("<Q", bad, 16, n)                     # medoid == n
+    cases["medoid"] = bad
+    bad = bytearray(raw)
+    bad[32 + 5 * bpn + 2 * dim] = R + 1                    # count > R
+    cases["count"] = bad
+    bad = bytearray(raw)
+    o = 32 + 7 * bpn + 2 * dim
+    assert bad[o] > 0
+    struct.pack_into("<I", bad, o + 1, n)                  # first edge id == n
+    cases["edge"] = bad
+    for name, data in cases.items():
+        q = tmp_path / f"{name}.graph"
+        q.write_bytes(bytes(data))
+        with pytest.raises((OSError, RuntimeError), match="medoid|edge count|neighbour id"):
+            load(q, dim, R)

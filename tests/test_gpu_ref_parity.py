@@ -1,0 +1,116 @@
+"""Parity with the reference's own CUDA build at a BASELINE configuration.
+
+Config 1 (100,000 x 128 N(0,1) rows, seed 0; 1,000 queries, seed 1; L2,
+R = 32, alpha = 1.2; k = 10).  The reference library is the unmodified
+reference compiled for sm_100a (oracle/_ref, called through its tvm_ffi ops,
+ffi/jasper_ffi_common.cuh:210-230,302-369):
+
+* search parity: the reference builds and saves a graph; this library loads
+  that file and searches it at beam widths 16..256 (limit 2 x bw); ids and
+  distance bits equal the reference's own search on the same handle.  The
+  other direction too: a graph built here, saved, loaded by the reference
+  and searched there, equals this library's search of it.
+* build parity: recall@10 of the graph built here is within 0.005 of the
+  reference-built graph's at every beam width, against an exact brute-force
+  ground truth.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from jasper_b200 import _lib, synthetic
+from oracle import oracle as O
+import jb_testlib as T
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+REF_LIB = ROOT / "oracle" / "_ref" / "lib" / "libjasper_ffi.so"
+BWS = (16, 32, 64, 128, 256)
+K = 10
+
+
+@pytest.fixture(scope="module")
+def ref(cuda):
+    tvm_ffi = pytest.importorskip("tvm_ffi")
+    if not REF_LIB.exists():
+        pytest.skip("reference library oracle/_ref not built (oracle/build_ref.sh)")
+    return tvm_ffi.load_module(str(REF_LIB))
+
+
+@pytest.fixture(scope="module")
+def config1():
+    X = synthetic.gaussian(100_000, 128, 0)
+    Q = synthetic.gaussian(1_000, 128, 1)
+    gt, _ = O.bruteforce_knn(X.astype(np.float32), Q.astype(np.float32), K)
+    return X, Q, gt
+
+
+def ref_search(ref, h, Qd, bw):
+    import torch
+    oi = torch.empty(Qd.shape[0], K, dtype=torch.int32, device="cuda")
+    od = torch.empty(Qd.shape[0], K, dtype=torch.float32, device="cuda")
+    ref.jasper_search_f16_r32_l2(h, Qd, oi, od, K, bw, 2 * bw, False)
+    torch.cuda.synchronize()
+    return oi.cpu().numpy(), od.cpu().numpy()
+
+
+def recall(ids, gt):
+    return float(np.mean([len(set(a) & set(b)) for a, b in zip(ids.tolist(), gt.tolist())])) / K
+
+
+def load(path, dim, R):
+    h = C.c_int64(-1)
+    _lib.call("jb_graph_load", str(path).encode(), dim, R, 0, 0, C.byref(h))
+    return h.value
+
+
+def test_config1_search_and_build_match_reference(ref, config1, tmp_path):
+    import torch
+    import jasper_b200 as jasper
+    X, Q, gt = config1
+    Xd = torch.from_numpy(X).cuda()
+    Qd = torch.from_numpy(Q).cuda()
+
+    # the reference builds, saves; this library loads the file and searches it
+    rh = ref.jasper_construct_f16_r32_l2(Xd, 128, 1.2, 10 * 10**9, False)
+    ref_recall, our_recall = {}, {}
+    try:
+        rfile = tmp_path / "ref.graph"
+        ref.jasper_save_f16_r32_l2(rh, str(rfile))
+        h = load(rfile, 128, 32)
+        try:
+            for bw in BWS:
+                ri, rd = ref_search(ref, rh, Qd, bw)
+                ji, jd = T.search(h, Q, K, bw)
+                T.assert_same_results(ji, jd, ri, rd, msg=f"reference graph, bw={bw}")
+                ref_recall[bw] = recall(ri, gt)
+        finally:
+            T.free(h)
+    finally:
+        ref.jasper_free_graph(rh)
+
+    # this library builds (public API), saves; the reference loads and searches
+    g = jasper.Graph.build(Xd, n_neighbors=32, distance="l2", alpha=1.2)
+    try:
+        ofile = tmp_path / "ours.graph"
+        g.save(str(ofile))
+        rh = ref.jasper_load_f16_r32_l2(str(ofile), 128, False)
+        try:
+            for bw in BWS:
+                ji, jd = g.search(Qd, k=K, beam_width=bw)
+                ji, jd = ji.cpu().numpy(), jd.cpu().numpy()
+                ri, rd = ref_search(ref, rh, Qd, bw)
+                T.assert_same_results(ji, jd, ri, rd, msg=f"graph built here, bw={bw}")
+                our_recall[bw] = recall(ji, gt)
+        finally:
+            ref.jasper_free_graph(rh)
+    finally:
+        g.free()
+
+    for bw in BWS:
+        assert abs(our_recall[bw] - ref_recall[bw]) <= 0.005, (bw, our_recall, ref_recall)
+    assert ref_recall[64] > 0.9
