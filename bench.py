@@ -16,9 +16,18 @@ with host buffers (jb_graph_search_host: H2D queries, search, D2H results).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-With N > 1 (torchrun, one rank per GPU) each rank builds and searches its own
-1M-row shard with its own 10,000 queries (weak scaling: per-GPU work fixed,
-no data-path collective); times are the max over ranks.
+With N > 1 (torchrun, one rank per GPU) every rank holds the same config-2
+graph and searches its slice of the same 10,000 queries; the slices' top-k
+are gathered to rank 0 over NCCL inside each timed step (strong scaling),
+times are the max over ranks.  The run then adds the config-5 range-sharded
+leg (one 12.5M-row shard per GPU, queries broadcast, top-k gathered and
+merged; weak scaling) under "range_sharded".  After the timed region, rank 0
+at N = 1 also reports the CPU baselines and parity with the reference's own
+build (oracle/_ref) -- checkers, never on the timed path.
+
+Other modes: --mode config1 | directional (config 3) | rabitq (config 4) |
+sharded (config 5 alone) | rotation; --impl reference runs the reference's
+CUDA build on the same config (--ref-ndebug: its -DNDEBUG build).
 """
 from __future__ import annotations
 
@@ -167,6 +176,16 @@ def exact_gt(base: torch.Tensor, queries: torch.Tensor, k: int) -> torch.Tensor:
     return torch.cat(out)
 
 
+def exact_ip_gt(base: torch.Tensor, queries: torch.Tensor, k: int) -> torch.Tensor:
+    """Exact maximum-inner-product top-k on the GPU in fp32."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    out = []
+    for q0 in range(0, queries.size(0), 250):
+        s = queries[q0:q0 + 250].float() @ base.float().T
+        out.append(s.topk(k, dim=1).indices.int())
+    return torch.cat(out)
+
+
 def recall_at_k(res: torch.Tensor, gt: torch.Tensor) -> float:
     r = res.long()
     g = gt.long()
@@ -203,9 +222,23 @@ def load_data(n_base, n_q, rank=0):
 
 
 # ── jasper_b200 arm ───────────────────────────────────────────────────────
-def run_jasper(args):
-    import jasper_b200 as jasper
-    from jasper_b200 import _lib
+class stdout_to_stderr:
+    """Sends fd 1 to fd 2 while the reference library prints its progress,
+    so that this script's stdout carries only its JSON lines."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+
+
+def init_dist():
     ws, rank, local = dist_env()
     dist = None
     if ws > 1:
@@ -214,33 +247,68 @@ def run_jasper(args):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
-    dev = torch.device("cuda", torch.cuda.current_device())
-    base_np, q_np = load_data(args.n, args.nq, rank)
+    return ws, rank, dist, torch.device("cuda", torch.cuda.current_device())
+
+
+def max_over_ranks(dist, vals, dev):
+    t = torch.tensor(vals, device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def run_jasper(args):
+    """Config 2.  N = 1: one GPU searches all 10,000 queries.  N > 1: the
+    small-index mode -- every rank holds the same config-2 graph (replica)
+    and searches its contiguous slice of the same 10,000 queries; the
+    slices' top-k are gathered to rank 0 over NCCL inside the timed step
+    (strong scaling: total work fixed)."""
+    import jasper_b200 as jasper
+    from jasper_b200 import _lib, sharded
+    ws, rank, dist, dev = init_dist()
+    base_np, q_np = load_data(args.n, args.nq, 0)
     base = torch.from_numpy(base_np).to(dev)
     queries = torch.from_numpy(q_np).to(dev)
-    q_host = torch.from_numpy(q_np).pin_memory()
+    sl = sharded.split_queries(args.nq, ws, rank)
+    nloc_max = -(-args.nq // ws)
+    q_loc = queries[sl].contiguous()
+    nloc = q_loc.shape[0]
+    q_loc_host = torch.from_numpy(q_np[sl]).pin_memory()
 
-    # build (timed on the device)
+    # build (device time on every replica; max over ranks)
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     t0 = time.perf_counter()
     g = jasper.Graph.build(base, n_neighbors=64, distance="l2", alpha=1.2)
     torch.cuda.synchronize()
-    build_s = time.perf_counter() - t0
+    (build_s,) = max_over_ranks(dist, [time.perf_counter() - t0], dev)
 
     gt = exact_gt(base, queries, K)
-    recalls = {}
-    for bw in BWS:
-        ids, _ = g.search(queries, k=K, beam_width=bw)
+    recalls, full = {}, {}
+    for bw in BWS:     # every replica holds the same graph: identical sweeps
+        ids, dd = g.search(queries, k=K, beam_width=bw)
         recalls[bw] = recall_at_k(ids, gt)
+        full[bw] = (ids, dd)
     lo, hi = bracket(recalls)
-    if dist is not None:
-        t = torch.tensor([lo, hi], device=dev)
-        dist.broadcast(t, 0)
-        lo, hi = int(t[0]), int(t[1])
     pair = (lo, hi) if lo != hi else (hi,)
 
     flush = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream()
+    gbuf = (torch.empty(ws, 2, nloc_max, K, dtype=torch.int32, device=dev)
+            if ws > 1 and rank == 0 else None)
+    pad_i = torch.full((nloc_max, K), -1, dtype=torch.int32, device=dev)
+    pad_d = torch.full((nloc_max, K), 1e30, dtype=torch.float32, device=dev)
+
+    def one(bw):
+        ids, dd = g.search(q_loc, k=K, beam_width=bw)
+        if dist is None:
+            return ids, dd
+        if nloc < nloc_max:
+            pad_i[:nloc].copy_(ids)
+            pad_d[:nloc].copy_(dd)
+            ids, dd = pad_i, pad_d
+        return sharded.gather_topk(ids, dd, root=0, out=gbuf)
 
     def step(times):
         for bw in pair:
@@ -248,7 +316,7 @@ def run_jasper(args):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            g.search(queries, k=K, beam_width=bw)
+            one(bw)
             e1.record(stream)
             times[bw].append((e0, e1))
 
@@ -269,127 +337,245 @@ def run_jasper(args):
     if dist is not None:
         dist.barrier()
     torch.cuda.synchronize()
-    ms = {bw: sum(a.elapsed_time(b) for a, b in times[bw]) / args.steps for bw in pair}
+    ms_l = [sum(a.elapsed_time(b) for a, b in times[bw]) / args.steps for bw in pair]
+    ms = dict(zip(pair, max_over_ranks(dist, ms_l, dev)))
     total_ms = sum(ms.values())
-    if dist is not None:
-        t = torch.tensor([ms[bw] for bw in pair] + [total_ms, build_s], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        vals = t.tolist()
-        ms = {bw: vals[i] for i, bw in enumerate(pair)}
-        total_ms, build_s = vals[-2], vals[-1]
-    qps = {bw: ws * args.nq / (ms[bw] / 1e3) for bw in pair}
+    qps = {bw: args.nq / (ms[bw] / 1e3) for bw in pair}
     value = interp_qps(recalls[lo], qps[lo], recalls[hi], qps[hi])
 
-    # e2e: the C ABI with host buffers (copies in, search, copies out)
-    out_i = torch.empty(args.nq, K, dtype=torch.int32).pin_memory()
-    out_d = torch.empty(args.nq, K, dtype=torch.float32).pin_memory()
+    # the split-and-gathered results equal one GPU's search of all queries
+    split_ok = None
+    if dist is not None:
+        got = one(hi)
+        if rank == 0:
+            gi = torch.cat([got[0][r, :sharded.shard_range(args.nq, ws, r)[1]] for r in range(ws)])
+            gd = torch.cat([got[1][r, :sharded.shard_range(args.nq, ws, r)[1]] for r in range(ws)])
+            split_ok = bool(torch.equal(gi, full[hi][0]) and
+                            torch.equal(gd.view(torch.int32), full[hi][1].view(torch.int32)))
+
+    # e2e: the C ABI with host buffers (copies in, search, copies out), each
+    # rank on its slice; max over ranks of the median call
+    out_i = torch.empty(nloc, K, dtype=torch.int32).pin_memory()
+    out_d = torch.empty(nloc, K, dtype=torch.float32).pin_memory()
     e2e_ms = {}
     with ClockSampler(dev) as clk_e2e:
         for bw in pair:
             for _ in range(max(2, args.warmup)):
-                _lib.call("jb_graph_search_host", g._handle, q_host.data_ptr(), args.nq, 128,
+                _lib.call("jb_graph_search_host", g._handle, q_loc_host.data_ptr(), nloc, 128,
                           out_i.data_ptr(), out_d.data_ptr(), K, bw, 2 * bw, stream.cuda_stream)
             ts = []
             for _ in range(max(args.steps, 10)):
                 flush_l2(flush)
                 torch.cuda.synchronize()
+                if dist is not None:
+                    dist.barrier()
                 t1 = time.perf_counter()
-                _lib.call("jb_graph_search_host", g._handle, q_host.data_ptr(), args.nq, 128,
+                _lib.call("jb_graph_search_host", g._handle, q_loc_host.data_ptr(), nloc, 128,
                           out_i.data_ptr(), out_d.data_ptr(), K, bw, 2 * bw, stream.cuda_stream)
                 ts.append(time.perf_counter() - t1)
             e2e_ms[bw] = 1e3 * float(np.median(ts))
-    if dist is not None:
-        t = torch.tensor([e2e_ms[bw] for bw in pair], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = {bw: v for bw, v in zip(pair, t.tolist())}
-    e2e_qps = {bw: ws * args.nq / (e2e_ms[bw] / 1e3) for bw in pair}
+    e2e_ms = dict(zip(pair, max_over_ranks(dist, [e2e_ms[bw] for bw in pair], dev)))
+    e2e_qps = {bw: args.nq / (e2e_ms[bw] / 1e3) for bw in pair}
     e2e_value = interp_qps(recalls[lo], e2e_qps[lo], recalls[hi], e2e_qps[hi])
 
-    # roofline numerator: algorithmic bytes of the search at the upper width
-    # B_q = 2*dpad (query) + sum_expanded(1 + 4*deg) + 2*dpad*(distinct rows evaluated) + 8k
-    _, _, st = g.search_with_stats(queries, k=K, beam_width=hi, distinct=True)
+    # roofline numerator: algorithmic bytes of this rank's search at the upper
+    # width, B_q = 2*dpad (query) + sum_expanded(1 + 4*deg) + 2*dpad*(distinct
+    # rows evaluated) + 8k, over the search-only kernel time
+    _, _, st = g.search_with_stats(q_loc, k=K, beam_width=hi, distinct=True)
     st = st.long().cpu()
     dpad = 128
     bytes_q = (2 * dpad + st[:, 0] + 4 * st[:, 1] + 2 * dpad * st[:, 4] + 8 * K).sum().item()
+    kt = []
+    for _ in range(max(args.steps, 5)):
+        flush_l2(flush)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        g.search(q_loc, k=K, beam_width=hi)
+        b.record(stream)
+        kt.append((a, b))
+    torch.cuda.synchronize()
+    kernel_ms = float(np.mean([a.elapsed_time(b) for a, b in kt]))
     peak, peak_kind = measured_peaks()
-    achieved = bytes_q / (ms[hi] / 1e3) / 1e9
-    traffic = SEARCH_TRAFFIC.get((args.n, args.nq, hi))
+    achieved = bytes_q / (kernel_ms / 1e3) / 1e9
+    traffic = SEARCH_TRAFFIC.get((args.n, nloc, hi))
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic,
                 "traffic_source": "profiles/search_cfg2_bw32.md (dram__bytes_read.sum + "
                                   "dram__bytes_write.sum, one launch)" if traffic else None,
-                "algorithmic_bytes_per_launch": int(bytes_q),
+                "algorithmic_bytes_per_launch": int(bytes_q), "kernel_ms": round(kernel_ms, 4),
                 "peak_source": peak_kind, "kernel": f"beam_search_warp_kernel bw={hi}",
-                "bytes_per_query": round(bytes_q / args.nq, 1),
+                "queries_per_launch": nloc,
+                "bytes_per_query": round(bytes_q / nloc, 1),
                 "expansions_per_query": round(st[:, 0].float().mean().item(), 2),
                 "distinct_rows_per_query": round(st[:, 4].float().mean().item(), 2)}
 
-    cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(g, base_np, q_np, lo, hi, recalls, args)
+    cpu = parity = None
+    if rank == 0 and ws == 1:
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline(g, base_np, q_np, lo, hi, recalls, args)
+        if not args.no_parity:
+            parity = parity_leg(g, base, queries, gt, recalls, args)
+    g.free()
+    del base, queries, flush, gbuf, pad_i, pad_d, full
+    torch.cuda.empty_cache()
+
+    shard_res = None
+    if not args.no_sharded:
+        shard_res = sharded_leg(args, ws, rank, dist, dev)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "queries/s",
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(total_ms, 4), "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": round(total_ms, 4), "higher_is_better": True,
+            "scaling": "strong",
             "vs_baseline": None, "dtype": "f16 rows, f32 distances", "data": "synthetic",
             "config": {"workload": "config2: 1M x 128 SIFT-like fp16, L2, R=64, alpha=1.2, "
-                                   f"{args.nq} queries/GPU, k=10",
-                       "n_base": args.n, "queries_per_gpu": args.nq,
+                                   f"{args.nq} queries, k=10",
+                       "n_base": args.n, "queries": args.nq, "queries_per_gpu": nloc_max,
                        "bracket_beam_widths": list(pair), "limit": "2*beam_width",
-                       "parallelism": f"independent shards x{ws}" if ws > 1 else "single",
+                       "parallelism": (f"replicated graph x{ws}, queries split, top-k gathered "
+                                       "to rank 0 over NCCL inside the timed step")
+                       if ws > 1 else "single",
                        "l2": "flushed between timed searches (256 MB write)"},
             "recall_at_10": {str(b): round(r, 4) for b, r in recalls.items()},
             "qps": {str(b): round(v, 1) for b, v in qps.items()},
-            "build": {"mvec_per_s": round(ws * args.n / build_s / 1e6, 4),
+            "split_gather_identical_to_one_gpu": split_ok,
+            "build": {"mvec_per_s": round(args.n / build_s / 1e6, 4),
                       "seconds": round(build_s, 3),
-                      "note": (f"{ws} shards of {args.n} rows built concurrently, one per GPU; "
-                               "time = max over ranks") if ws > 1 else "single GPU"},
+                      "note": (f"the same graph built on each of {ws} replicas; time = max over "
+                               "ranks (build scaling: range_sharded)") if ws > 1 else "single GPU"},
             "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
                     "h2d_bytes_per_step": int(len(pair) * args.nq * 128 * 2),
                     "d2h_bytes_per_step": int(len(pair) * args.nq * K * 8),
-                    "timing": "median host wall time of jb_graph_search_host per call",
+                    "timing": ("median host wall time of jb_graph_search_host per call"
+                               + (" on each rank's query slice, max over ranks" if ws > 1 else "")),
                     "clocks": clk_e2e.summary()},
             "roofline": roofline,
             "cpu_baseline": cpu,
+            "parity_vs_reference": parity,
+            "range_sharded": shard_res,
             "gpu_launches": args.steps * len(pair),
             "clocks": clk.summary(),
             "wall_s_timed": round(wall, 3),
         }
         print(json.dumps(line), flush=True)
-    g.free()
     if dist is not None:
         dist.destroy_process_group()
 
 
 def cpu_baseline(g, base_np, q_np, lo, hi, recalls, args):
-    """The CPU restatement of the reference search (oracle/, a port) timed on
-    this host's cores, on a bounded sample of the same queries."""
+    """The CPU baselines on this host's cores, on bounded samples of the same
+    queries.  Headline: exact brute-force k-NN (oracle/bruteforce.c: fp16
+    rows widened to fp32, all host threads, per-thread top-k; recall 1 by
+    construction).  Beside it: the CPU restatement of the reference's beam
+    search on this graph (a correctness oracle, timed for information)."""
     from oracle import oracle as O
     from jasper_b200 import _lib
+    cores = os.cpu_count() or 1
+    bf_base = base_np.astype(np.float32)
+    bf_q = q_np.astype(np.float32)
+    t0 = time.perf_counter()
+    O.bruteforce_knn(bf_base, bf_q[:4 * cores], K, threads=cores)
+    est = 4 * cores / (time.perf_counter() - t0)
+    m = int(min(q_np.shape[0], max(4 * cores, est * args.cpu_seconds)))
+    t0 = time.perf_counter()
+    bi, _ = O.bruteforce_knn(bf_base, bf_q[:m], K, threads=cores)
+    bf_qps = m / (time.perf_counter() - t0)
+    exact = exact_gt(torch.from_numpy(base_np).cuda(), torch.from_numpy(q_np[:m]).cuda(), K)
+    bf_recall = recall_at_k(torch.from_numpy(bi), exact.cpu())
+    del bf_base
+
     n, R = base_np.shape[0], 64
     og = O.OracleGraph(base_np, R)
     _lib.call("jb_graph_get_edges", g._handle, og.edges.ctypes.data, og.edist.ctypes.data,
               og.counts.ctypes.data)
-    cores = O.max_threads()
     O.set_threads(cores)
-    out = {}
-    budget_s = args.cpu_seconds / (2 if lo != hi else 1)
+    port = {}
+    budget_s = args.cpu_seconds / 2 / (2 if lo != hi else 1)
     for bw in sorted({lo, hi}):
         done, t_used = 0, 0.0
-        sample = 500
         while t_used < budget_s and done < q_np.shape[0]:
-            qs = q_np[done:done + sample]
+            qs = q_np[done:done + 500]
             t0 = time.perf_counter()
             og.search(qs, K, bw, 2 * bw)
             t_used += time.perf_counter() - t0
             done += qs.shape[0]
-        out[bw] = done / t_used
-    qps = interp_qps(recalls[lo], out[lo], recalls[hi], out[hi])
-    return {"value": round(qps, 1), "unit": "queries/s", "cores": cores, "kind": "port",
-            "sample": f"first queries of the same set until ~{args.cpu_seconds:.0f} s of CPU time "
-                      f"per run, beam widths {sorted({lo, hi})}, all host threads"}
+        port[bw] = done / t_used
+    return {"value": round(bf_qps, 1), "unit": "queries/s", "cores": cores, "kind": "port",
+            "algorithm": "exact brute-force k-NN (oracle/bruteforce.c), fp16 rows as fp32",
+            "recall_at_10": round(bf_recall, 4),
+            "sample": f"the first {m} of the {q_np.shape[0]} queries against all "
+                      f"{base_np.shape[0]} rows (~{args.cpu_seconds:.0f} s), {cores} threads",
+            "beam_search_port": {
+                "value": round(interp_qps(recalls[lo], port[lo], recalls[hi], port[hi]), 1),
+                "unit": "queries/s", "cores": cores,
+                "note": "CPU restatement of the reference's beam search on this graph "
+                        f"(a correctness oracle), beam widths {sorted({lo, hi})}"}}
+
+
+def parity_leg(g, base, queries, gt, recalls, args):
+    """The checker, after the timed region: parity with the reference's own
+    CUDA build (oracle/_ref) on config 2.  (1) Same graph: this graph is
+    saved, loaded by the reference, and searched there at every beam width;
+    its ids and distance bits are compared with this library's search.
+    (2) Build: the reference builds its own graph from the same rows; its
+    recall@10 at every width is set beside this build's."""
+    lib = ROOT / "oracle" / "_ref" / "lib" / "libjasper_ffi.so"
+    try:
+        import tvm_ffi
+    except ImportError:
+        return {"unavailable": "tvm_ffi not importable"}
+    if not lib.exists():
+        return {"unavailable": "reference library oracle/_ref not built"}
+    import tempfile
+    mod = tvm_ffi.load_module(str(lib))
+    nq = queries.shape[0]
+    oi = torch.empty(nq, K, dtype=torch.int32, device=queries.device)
+    od = torch.empty(nq, K, dtype=torch.float32, device=queries.device)
+    mism, total, max_rel = 0, 0, 0.0
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "g.graph")
+        g.save(path)
+        with stdout_to_stderr():
+            rh = mod.jasper_load_f16_r64_l2(path, 128, False)
+    try:
+        for bw in BWS:
+            ji, jd = g.search(queries, k=K, beam_width=bw)
+            with stdout_to_stderr():
+                mod.jasper_search_f16_r64_l2(rh, queries, oi, od, K, bw, 2 * bw, False)
+            torch.cuda.synchronize()
+            bad = (ji != oi).any(1) | (jd.view(torch.int32) != od.view(torch.int32)).any(1)
+            mism += int(bad.sum())
+            total += nq
+            rel = ((jd - od).abs() / od.abs().clamp(min=1e-30)).max().item()
+            max_rel = max(max_rel, rel)
+    finally:
+        mod.jasper_free_graph(rh)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with stdout_to_stderr():
+        rh = mod.jasper_construct_f16_r64_l2(base, 128, 1.2, 10 * 10**9, False)
+    torch.cuda.synchronize()
+    ref_build_s = time.perf_counter() - t0
+    ref_rec = {}
+    try:
+        for bw in BWS:
+            with stdout_to_stderr():
+                mod.jasper_search_f16_r64_l2(rh, queries, oi, od, K, bw, 2 * bw, False)
+            torch.cuda.synchronize()
+            ref_rec[bw] = recall_at_k(oi, gt)
+    finally:
+        mod.jasper_free_graph(rh)
+    diff = max(abs(recalls[bw] - ref_rec[bw]) for bw in BWS)
+    return {"same_graph_search": {"mismatched_queries": mism, "query_searches": total,
+                                  "beam_widths": list(BWS), "max_rel_dist_err": max_rel,
+                                  "compare": "ids and distance bits, this build's graph searched "
+                                             "by the reference (jasper_search_f16_r64_l2)"},
+            "build_recall": {"reference": {str(b): round(r, 4) for b, r in ref_rec.items()},
+                             "here": {str(b): round(r, 4) for b, r in recalls.items()},
+                             "max_abs_diff": round(diff, 4), "within_0.005": diff <= 0.005},
+            "reference_build_s": round(ref_build_s, 3)}
 
 
 # ── config 5: range-sharded index (one shard per GPU) ─────────────────────
@@ -434,21 +620,13 @@ def exact_topk_shard(base: torch.Tensor, queries: torch.Tensor, k: int, offset: 
     return torch.cat(out_i), torch.cat(out_d)
 
 
-def run_sharded(args):
+def sharded_leg(args, ws, rank, dist, dev):
     """Config 5: every rank builds a range shard of args.n_shard rows (global
     ids rank * n_shard + i) concurrently; each query batch goes to every
-    rank, per-shard top-k are gathered to rank 0 over NCCL and merged there
-    (jb_merge_topk).  Weak scaling: the index grows with the number of GPUs."""
+    rank, per-shard top-k are gathered to rank 0 with one NCCL gather and
+    merged there (jb_merge_topk_strided).  Weak scaling: the index grows
+    with the number of GPUs.  Returns the result dict on rank 0."""
     from jasper_b200 import sharded
-    ws, rank, local = dist_env()
-    dist = None
-    if ws > 1:
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    else:
-        torch.cuda.set_device(0)
-    dev = torch.device("cuda", torch.cuda.current_device())
     n_shard = args.n_shard
     n_total = n_shard * ws
     offset = rank * n_shard
@@ -461,12 +639,6 @@ def run_sharded(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(vals):
-        t = torch.tensor(vals, device=dev, dtype=torch.float64)
-        if dist is not None:
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return t.tolist()
-
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -474,7 +646,14 @@ def run_sharded(args):
                                     alpha=1.2)
     e1.record()
     barrier()
-    (build_s,) = max_over_ranks([e0.elapsed_time(e1) / 1e3])
+    own_build_s = e0.elapsed_time(e1) / 1e3
+    (build_s,) = max_over_ranks(dist, [own_build_s], dev)
+    build_each = [own_build_s]
+    if dist is not None:
+        t = torch.zeros(ws, device=dev, dtype=torch.float64)
+        t[rank] = own_build_s
+        dist.all_reduce(t)
+        build_each = t.tolist()
 
     gi, gd = exact_topk_shard(base, queries, K, offset)
     if ws > 1:
@@ -482,17 +661,18 @@ def run_sharded(args):
         gt = sharded.merge_topk(got[0], got[1])[0] if rank == 0 else None
     else:
         gt = gi
+    del base
+    torch.cuda.empty_cache()
 
-    def search(bw):
+    def search(bw, phases=None):
         if ws > 1:
-            return sg.search(queries, k=K, beam_width=bw, root=0)
+            return sg.search(queries, k=K, beam_width=bw, root=0, phases=phases)
         return sg.search_local(queries, k=K, beam_width=bw)
 
     recalls = {}
     for bw in BWS:
         res = search(bw)
-        r = recall_at_k(res[0], gt) if rank == 0 else 0.0
-        recalls[bw] = r
+        recalls[bw] = recall_at_k(res[0], gt) if rank == 0 else 0.0
     t = torch.tensor([recalls[bw] for bw in BWS], device=dev, dtype=torch.float64)
     if dist is not None:
         dist.broadcast(t, 0)
@@ -505,26 +685,45 @@ def run_sharded(args):
             search(bw)
     barrier()
     times = {bw: [] for bw in pair}
+    phases = {bw: [] for bw in pair}
     with ClockSampler(dev) as clk:
         for _ in range(args.steps):
             for bw in pair:
                 a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 a.record(stream)
-                search(bw)
+                search(bw, phases[bw] if ws > 1 else None)
                 b.record(stream)
                 times[bw].append((a, b))
         torch.cuda.synchronize()
     barrier()
     ms_local = [sum(x.elapsed_time(y) for x, y in times[bw]) / args.steps for bw in pair]
-    ms = dict(zip(pair, max_over_ranks(ms_local)))
+    ms = dict(zip(pair, max_over_ranks(dist, ms_local, dev)))
     qps = {bw: args.nq / (ms[bw] / 1e3) for bw in pair}
     value = interp_qps(recalls[lo], qps[lo], recalls[hi], qps[hi])
+    # per phase (median over steps): local search, gather (includes waiting
+    # for the slowest shard), merge; every rank's numbers
+    phase_ms = None
+    if ws > 1:
+        loc = []
+        for bw in pair:
+            ev = phases[bw]
+            loc += [float(np.median([e[0].elapsed_time(e[1]) for e in ev])),
+                    float(np.median([e[1].elapsed_time(e[2]) for e in ev])),
+                    float(np.median([e[2].elapsed_time(e[3]) for e in ev]))]
+        t = torch.zeros(ws, len(loc), device=dev, dtype=torch.float64)
+        t[rank] = torch.tensor(loc, dtype=torch.float64)
+        dist.all_reduce(t)
+        allp = t.tolist()
+        phase_ms = {}
+        for i, bw in enumerate(pair):
+            phase_ms[str(bw)] = {
+                "search_ms_by_rank": [round(r[3 * i], 4) for r in allp],
+                "gather_ms_by_rank": [round(r[3 * i + 1], 4) for r in allp],
+                "merge_ms_rank0": round(allp[0][3 * i + 2], 4)}
 
     # e2e: queries from pinned host memory, the merged top-k back to the host
     q_host = queries.cpu().pin_memory()
     e2e = {}
-    clk_e2e = ClockSampler(dev)
-    clk_e2e.__enter__()
     for bw in pair:
         ts = []
         for it in range(max(args.steps, 10) + args.warmup):
@@ -539,40 +738,52 @@ def run_sharded(args):
             if it >= args.warmup:
                 ts.append(time.perf_counter() - t1)
         e2e[bw] = float(np.median(ts)) * 1e3
-    clk_e2e.__exit__(None, None, None)
-    e2e = dict(zip(pair, max_over_ranks([e2e[bw] for bw in pair])))
+    e2e = dict(zip(pair, max_over_ranks(dist, [e2e[bw] for bw in pair], dev)))
     e2e_qps = {bw: args.nq / (e2e[bw] / 1e3) for bw in pair}
     e2e_value = interp_qps(recalls[lo], e2e_qps[lo], recalls[hi], e2e_qps[hi])
-
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "queries/s", "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sum(ms.values()), 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 rows, f32 distances", "data": "synthetic",
-            "config": {"workload": f"config5: range-sharded {n_total} x 128 SIFT-like fp16 "
-                                   f"({ws} shards x {n_shard}), L2, R=64, alpha=1.2, "
-                                   f"{args.nq} queries broadcast, k=10, NCCL gather + device merge",
-                       "n_base": n_total, "rows_per_gpu": n_shard, "queries": args.nq,
-                       "bracket_beam_widths": list(pair), "limit": "2*beam_width",
-                       "parallelism": f"range shards x{ws}",
-                       "l2": "inputs larger than L2 (3.2 GB of rows per GPU)"},
-            "recall_at_10": {str(b): round(r, 4) for b, r in recalls.items()},
-            "qps": {str(b): round(v, 1) for b, v in qps.items()},
-            "build": {"mvec_per_s": round(n_total / build_s / 1e6, 4),
-                      "seconds": round(build_s, 3),
-                      "note": f"{ws} shards built concurrently; time = max over ranks"},
-            "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
-                    "h2d_bytes_per_step": int(len(pair) * args.nq * 128 * 2),
-                    "d2h_bytes_per_step": int(len(pair) * args.nq * K * 8),
-                    "timing": "median host wall time per query batch (upload, search on "
-                              "every shard, gather, merge, download), max over ranks",
-                    "clocks": clk_e2e.summary()},
-            "gpu_launches": args.steps * len(pair) * (2 if ws > 1 else 1),
-            "clocks": clk.summary(),
-        }
-        print(json.dumps(line), flush=True)
     sg.free()
+    del queries, gi, gd
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    return {
+        "value": round(value, 1), "unit": "queries/s", "n_gpus": ws, "scaling": "weak",
+        "ms_per_step": round(sum(ms.values()), 4),
+        "workload": f"config5: range-sharded {n_total} x 128 SIFT-like fp16 ({ws} shards x "
+                    f"{n_shard}), L2, R=64, alpha=1.2, {args.nq} queries broadcast, k=10, one "
+                    "NCCL gather + device merge",
+        "rows_per_gpu": n_shard, "bracket_beam_widths": list(pair),
+        "recall_at_10": {str(b): round(r, 4) for b, r in recalls.items()},
+        "qps": {str(b): round(v, 1) for b, v in qps.items()},
+        "phases": phase_ms,
+        "build": {"mvec_per_s": round(n_total / build_s / 1e6, 4), "seconds": round(build_s, 3),
+                  "seconds_by_rank": [round(x, 3) for x in build_each],
+                  "note": f"{ws} shards built concurrently; time = max over ranks"},
+        "e2e": {"value": round(e2e_value, 1), "unit": "queries/s",
+                "h2d_bytes_per_step": int(len(pair) * args.nq * 128 * 2),
+                "d2h_bytes_per_step": int(len(pair) * args.nq * K * 8),
+                "timing": "median host wall time per query batch (upload, search on every "
+                          "shard, gather, merge, download), max over ranks"},
+        "gpu_launches": args.steps * len(pair) * (2 if ws > 1 else 1),
+        "clocks": clk.summary(),
+    }
+
+
+def run_sharded(args):
+    """--mode sharded: the config-5 leg alone, as its own JSON line."""
+    ws, rank, dist, dev = init_dist()
+    r = sharded_leg(args, ws, rank, dist, dev)
+    if rank == 0:
+        line = {"metric": METRIC, "value": r["value"], "unit": r["unit"], "n_gpus": ws,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms_per_step"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f16 rows, f32 distances", "data": "synthetic",
+                "config": {"workload": r["workload"], "n_base": r["rows_per_gpu"] * ws,
+                           "rows_per_gpu": r["rows_per_gpu"], "queries": args.nq,
+                           "parallelism": f"range shards x{ws}",
+                           "l2": "inputs larger than L2 (3.2 GB of rows per GPU)"}}
+        line.update({k: v for k, v in r.items() if k not in line and k != "workload"})
+        print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
 
@@ -704,12 +915,7 @@ def run_rabitq(args):
     n = args.n
     X = gen_relu_sphere_gpu(n, 960, 256, 0.3, 6, 6, dev)
     Q = gen_relu_sphere_gpu(1000, 960, 256, 0.3, 7, 6, dev)
-    torch.backends.cuda.matmul.allow_tf32 = False
-    sims = []
-    for q0 in range(0, 1000, 250):
-        s = Q[q0:q0 + 250].float() @ X.float().T
-        sims.append(s.topk(K, dim=1).indices.int())
-    gt = torch.cat(sims)
+    gt = exact_ip_gt(X, Q, K)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     g = jasper.Graph.build(X, n_neighbors=64, distance="ip", alpha=1.0, build_rabitq=True)
@@ -719,7 +925,7 @@ def run_rabitq(args):
             "build": {"seconds": round(build_s, 3), "mvec_per_s": round(n / build_s / 1e6, 4),
                       "note": "graph construction + prerotation + RaBitQ codes"}}
     from jasper_b200 import _lib
-    for bw in (64, 128, 256):
+    for bw in (64, 128, 256, 512):
         # margin 1e30: the filter never drops anything (the exact search)
         for name, margin in (("rabitq", 1.0), ("exact", 1e30)):
             ids, _ = g.rabitq_search(Q, k=K, beam_width=bw, margin=margin)
@@ -735,76 +941,205 @@ def run_rabitq(args):
             line[f"{name}_bw{bw}"] = {"recall_at_10": round(recall_at_k(ids, gt), 4),
                                       "qps": round(qps, 1), "ms": round(ms, 4),
                                       "rows_read_per_query": round(st[:, 2].float().mean().item(), 1)}
-    print(json.dumps(line), flush=True)
     g.free()
+    for name in ("rabitq", "exact"):
+        rec = {bw: line[f"{name}_bw{bw}"]["recall_at_10"] for bw in (64, 128, 256, 512)}
+        qp = {bw: line[f"{name}_bw{bw}"]["qps"] for bw in (64, 128, 256, 512)}
+        lo, hi = bracket(rec)
+        line[f"{name}_qps_at_0.95"] = (round(interp_qps(rec[lo], qp[lo], rec[hi], qp[hi]), 1)
+                                       if rec[hi] >= TARGET else None)
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = bruteforce_baseline(X.cpu().numpy(), Q.cpu().numpy(), 1, gt.cpu(),
+                                                   args)
+    print(json.dumps(line), flush=True)
+
+
+def bruteforce_baseline(base_np, q_np, metric, gt, args):
+    """Exact brute-force k-NN on all host cores (oracle/bruteforce.c, fp16
+    rows as fp32) over a bounded prefix of the queries."""
+    from oracle import oracle as O
+    cores = os.cpu_count() or 1
+    b = base_np.astype(np.float32)
+    q = q_np.astype(np.float32)
+    t0 = time.perf_counter()
+    O.bruteforce_knn(b, q[:cores], K, metric, threads=cores)
+    est = cores / (time.perf_counter() - t0)
+    m = int(min(q.shape[0], max(cores, est * args.cpu_seconds)))
+    t0 = time.perf_counter()
+    ids, _ = O.bruteforce_knn(b, q[:m], K, metric, threads=cores)
+    qps = m / (time.perf_counter() - t0)
+    return {"value": round(qps, 1), "unit": "queries/s", "cores": cores, "kind": "port",
+            "algorithm": "exact brute-force k-NN (oracle/bruteforce.c), fp16 rows as fp32",
+            "recall_at_10": round(recall_at_k(torch.from_numpy(ids), gt[:m]), 4),
+            "sample": f"the first {m} of the {q.shape[0]} queries against all {b.shape[0]} rows "
+                      f"(~{args.cpu_seconds:.0f} s), {cores} threads"}
+
+
+def run_config1(args):
+    """Config 1: 100k x 128 N(0,1) rows (seed 0), 1k queries (seed 1), L2,
+    R = 32, alpha = 1.2, k = 10, beam widths 16..256 (the config names 64).
+    The index (25.6 MB of rows + 12.8 MB of ids) stays in the 126 MB L2, so
+    the search's bytes are set against an L2 read bandwidth measured here
+    (a torch reduction over an L2-resident 48 MB buffer)."""
+    import jasper_b200 as jasper
+    from jasper_b200 import synthetic
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    X = synthetic.gaussian(100_000, 128, 0)
+    Q = synthetic.gaussian(1000, 128, 1)
+    Xd = torch.from_numpy(X).to(dev)
+    Qd = torch.from_numpy(Q).to(dev)
+    gt = exact_gt(Xd, Qd, K)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    g = jasper.Graph.build(Xd, n_neighbors=32, distance="l2", alpha=1.2)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    # L2 read bandwidth: sum over a 48 MB buffer that stays in L2
+    buf = torch.ones(12 * 1024 * 1024, dtype=torch.float32, device=dev)
+    for _ in range(5):
+        buf.sum()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(50):
+        buf.sum()
+    b.record()
+    torch.cuda.synchronize()
+    l2_gbs = 50 * buf.numel() * 4 / (a.elapsed_time(b) / 1e3) / 1e9
+    del buf
+    line = {"mode": "config1", "config": "config1", "rows": 100_000, "dim": 128, "R": 32,
+            "build": {"seconds": round(build_s, 3), "mvec_per_s": round(0.1 / build_s, 4)},
+            "l2_read_gbs_measured": round(l2_gbs, 1)}
+    for bw in BWS:
+        ids, _ = g.search(Qd, k=K, beam_width=bw)
+        qps, ms = _timed_qps(lambda: g.search(Qd, k=K, beam_width=bw), 1000, args.steps,
+                             args.warmup)
+        _, _, st = g.search_with_stats(Qd, k=K, beam_width=bw, distinct=True)
+        st = st.long().cpu()
+        bytes_q = (2 * 128 + st[:, 0] + 4 * st[:, 1] + 2 * 128 * st[:, 4] + 8 * K).sum().item()
+        gbs = bytes_q / (ms / 1e3) / 1e9
+        line[f"bw{bw}"] = {"recall_at_10": round(recall_at_k(ids, gt), 4), "qps": round(qps, 1),
+                           "ms": round(ms, 4), "algorithmic_gbs": round(gbs, 1),
+                           "frac_of_l2_read": round(gbs / l2_gbs, 4)}
+    g.free()
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = bruteforce_baseline(X, Q, 0, gt.cpu(), args)
+    print(json.dumps(line), flush=True)
 
 
 # ── reference arm ─────────────────────────────────────────────────────────
+def ref_library(args):
+    name = "libjasper_ffi_ndebug.so" if args.ref_ndebug else "libjasper_ffi.so"
+    return ROOT / "oracle" / "_ref" / "lib" / name
+
+
+def ref_plain_sweep(mod, cfg, base, queries, dim, alpha, bws, gt, args):
+    """The reference's own build + search (tvm_ffi ops) for one plain config:
+    build time, recall@10 per beam width, wall-clock QPS per width (its call
+    includes its per-call cudaMalloc and stream sync), L2 flushed between
+    timed calls.  Returns (build_s, recalls, qps, clocks)."""
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with stdout_to_stderr():
+        h = getattr(mod, f"jasper_construct_{cfg}")(base, dim, alpha, 10 * 10**9, False)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    search = getattr(mod, f"jasper_search_{cfg}")
+    nq = queries.shape[0]
+    oi = torch.empty(nq, K, dtype=torch.int32, device="cuda")
+    od = torch.empty(nq, K, dtype=torch.float32, device="cuda")
+    flush = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
+    recalls, qps = {}, {}
+    try:
+        with ClockSampler(torch.device("cuda", torch.cuda.current_device())) as clk:
+            for bw in bws:
+                search(h, queries, oi, od, K, bw, 2 * bw, False)
+                torch.cuda.synchronize()
+                recalls[bw] = recall_at_k(oi, gt)
+                for _ in range(args.warmup):
+                    search(h, queries, oi, od, K, bw, 2 * bw, False)
+                ts = []
+                for _ in range(args.steps):
+                    flush_l2(flush)
+                    torch.cuda.synchronize()
+                    t1 = time.perf_counter()
+                    search(h, queries, oi, od, K, bw, 2 * bw, False)
+                    torch.cuda.synchronize()
+                    ts.append(time.perf_counter() - t1)
+                qps[bw] = nq / float(np.mean(ts))
+    finally:
+        mod.jasper_free_graph(h)
+    return build_s, recalls, qps, clk.summary()
+
+
 def run_reference(args):
+    """The reference's own CUDA implementation (unmodified sources compiled
+    for sm_100a, oracle/_ref) through its tvm_ffi ops, on the config the
+    other arm runs: config 2 by default, config 1 (--mode config1),
+    config 4's plain inner-product search (--mode rabitq; the reference has
+    no RaBitQ search), config 3 (--mode directional)."""
     ws, rank, local = dist_env()
     if rank != 0:
         return
-    lib = ROOT / "oracle" / "_ref" / "lib" / "libjasper_ffi.so"
+    lib = ref_library(args)
     if not lib.exists():
         print(json.dumps({"impl": "reference", "unavailable":
-                          "reference library oracle/_ref/lib/libjasper_ffi.so was not built"}))
+                          f"reference library {lib.relative_to(ROOT)} was not built"}))
         return
     import tvm_ffi
     torch.cuda.set_device(local if ws > 1 else 0)
     mod = tvm_ffi.load_module(str(lib))
-    base_np, q_np = load_data(args.n, args.nq, 0)
-    base = torch.from_numpy(base_np).cuda()
-    queries = torch.from_numpy(q_np).cuda()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    h = mod.jasper_construct_f16_r64_l2(base, 128, 1.2, 10 * 10**9, False)
-    torch.cuda.synchronize()
-    build_s = time.perf_counter() - t0
-    gt = exact_gt(base, queries, K)
-    search = mod.jasper_search_f16_r64_l2
-    oi = torch.empty(args.nq, K, dtype=torch.int32, device="cuda")
-    od = torch.empty(args.nq, K, dtype=torch.float32, device="cuda")
-    recalls = {}
-    for bw in BWS:
-        search(h, queries, oi, od, K, bw, 2 * bw, False)
-        torch.cuda.synchronize()
-        recalls[bw] = recall_at_k(oi, gt)
+    variant = ("-DNDEBUG build (device asserts compiled out)" if args.ref_ndebug
+               else "default build (device asserts on, as the reference ships)")
+    if args.mode == "directional":
+        return run_reference_directional(args, mod, variant)
+    if args.mode == "config1":
+        from jasper_b200 import synthetic
+        base = torch.from_numpy(synthetic.gaussian(100_000, 128, 0)).cuda()
+        queries = torch.from_numpy(synthetic.gaussian(1000, 128, 1)).cuda()
+        cfg, dim, alpha, bws = "f16_r32_l2", 128, 1.2, BWS
+        workload = ("config1: 100k x 128 N(0,1) fp16, L2, R=32, alpha=1.2, 1000 queries, k=10")
+        gt = exact_gt(base, queries, K)
+    elif args.mode == "rabitq":
+        dev = torch.device("cuda", torch.cuda.current_device())
+        base = gen_relu_sphere_gpu(args.n, 960, 256, 0.3, 6, 6, dev)
+        queries = gen_relu_sphere_gpu(1000, 960, 256, 0.3, 7, 6, dev)
+        cfg, dim, alpha, bws = "f16_r64_ip", 960, 1.0, (64, 128, 256, 512)
+        workload = (f"config4 (plain IP search; the reference has no RaBitQ search): {args.n} x "
+                    "960 ReLU-sphere fp16, IP, R=64, alpha=1.0, 1000 queries, k=10")
+        gt = exact_ip_gt(base, queries, K)
+    else:
+        base_np, q_np = load_data(args.n, args.nq, 0)
+        base = torch.from_numpy(base_np).cuda()
+        queries = torch.from_numpy(q_np).cuda()
+        cfg, dim, alpha, bws = "f16_r64_l2", 128, 1.2, BWS
+        workload = ("config2: 1M x 128 SIFT-like fp16, L2, R=64, alpha=1.2, "
+                    f"{args.nq} queries, k=10")
+        gt = exact_gt(base, queries, K)
+    nq = queries.shape[0]
+    n = base.shape[0]
+    build_s, recalls, qps, clk = ref_plain_sweep(mod, cfg, base, queries, dim, alpha, bws, gt,
+                                                 args)
     lo, hi = bracket(recalls)
     pair = (lo, hi) if lo != hi else (hi,)
-    flush = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device="cuda")
-    for _ in range(args.warmup):
-        for bw in pair:
-            search(h, queries, oi, od, K, bw, 2 * bw, False)
-    torch.cuda.synchronize()
-    ts = {bw: [] for bw in pair}
-    with ClockSampler(torch.device("cuda", 0)) as clk:
-        for _ in range(args.steps):
-            for bw in pair:
-                flush_l2(flush)
-                torch.cuda.synchronize()
-                t1 = time.perf_counter()
-                search(h, queries, oi, od, K, bw, 2 * bw, False)
-                torch.cuda.synchronize()
-                ts[bw].append(time.perf_counter() - t1)
-    ms = {bw: 1e3 * float(np.mean(ts[bw])) for bw in pair}
-    qps = {bw: args.nq / (ms[bw] / 1e3) for bw in pair}
+    reached = recalls[hi] >= TARGET
     value = interp_qps(recalls[lo], qps[lo], recalls[hi], qps[hi])
-    mod.jasper_free_graph(h)
+    ms = {bw: 1e3 * nq / qps[bw] for bw in pair}
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "queries/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(sum(ms.values()), 4), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(sum(ms.values()), 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16 rows, f32 distances", "data": "synthetic",
-        "config": {"workload": "config2: 1M x 128 SIFT-like fp16, L2, R=64, alpha=1.2, "
-                               f"{args.nq} queries, k=10",
-                   "n_base": args.n, "queries_per_gpu": args.nq, "bracket_beam_widths": list(pair),
-                   "limit": "2*beam_width", "parallelism": "single",
-                   "l2": "flushed between timed searches (256 MB write)",
+        "config": {"workload": workload, "n_base": n, "queries": nq,
+                   "bracket_beam_widths": list(pair), "limit": "2*beam_width",
+                   "parallelism": "single", "l2": "flushed between timed searches (256 MB write)",
                    "implementation": "unmodified reference CUDA sources (ffi/*.cu) compiled for "
-                                     "sm_100a by oracle/build_ref.sh, called through its tvm_ffi ops"},
+                                     f"sm_100a by oracle/build_ref.sh, {variant}, called "
+                                     "through its tvm_ffi ops"},
         "recall_at_10": {str(b): round(r, 4) for b, r in recalls.items()},
         "qps": {str(b): round(v, 1) for b, v in qps.items()},
-        "build": {"mvec_per_s": round(args.n / build_s / 1e6, 4), "seconds": round(build_s, 3)},
+        "recall_0.95_reached": reached,
+        "build": {"mvec_per_s": round(n / build_s / 1e6, 4), "seconds": round(build_s, 3)},
         "cpu_baseline": {"value": round(value, 1), "unit": "queries/s", "cores": 0,
                          "kind": "reference",
                          "sample": "the reference ships no CPU search: this arm runs its own "
@@ -812,9 +1147,76 @@ def run_reference(args):
                                    "per-call cudaMalloc and stream sync)"},
         "e2e": {"value": round(value, 1), "unit": "queries/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "clocks": clk.summary(),
+        "clocks": clk,
     }
     print(json.dumps(line), flush=True)
+
+
+def run_reference_directional(args, mod, variant):
+    """Config 3 on the reference: its own prerotated directional build
+    (seed 4) and PQ codebooks (k-means 20 iterations, seed 5; M = k_ranks,
+    the only PQ the reference has); its LSH payload builder is not run (it
+    stops on a failing device assert on this GPU), so the LSH payload is
+    computed by the CPU restatement (oracle/directional.py) on the
+    reference's own graph and rows.  Graph, payloads and PQ codebooks go
+    into a legacy-layout directional file that the reference loads and
+    searches with directional_search / pq_search."""
+    import tempfile
+    from jasper_b200 import synthetic
+    from oracle import directional as D
+    X = synthetic.gaussian(100_000, 128, 0)
+    Q = synthetic.gaussian(1000, 128, 1)
+    Xd = torch.from_numpy(X).cuda()
+    Qd = torch.from_numpy(Q).cuda()
+    gt = exact_gt(Xd, Qd, K)
+    for kr in (4, 16):
+        cfg = f"f16_r32_l2_k{kr}_d128"
+        with stdout_to_stderr():
+            h = getattr(mod, f"jasper_construct_directional_{cfg}")(Xd.clone(), 128, 1.2,
+                                                                   10 * 10**9, False, True, 4)
+            getattr(mod, f"jasper_build_pq_{cfg}")(h, 40000, 20, 5)
+        with tempfile.TemporaryDirectory() as td:
+            p1 = os.path.join(td, "g.graph")
+            with stdout_to_stderr():
+                getattr(mod, f"jasper_save_directional_{cfg}")(h, p1)
+            mod.jasper_free_graph(h)
+            rows, edges, edist, counts, medoid, pq = D.read_directional_file(p1, 128, 32)
+            packed, mag = D.lsh_edges(rows, edges, counts, kr)
+            c, nd = D.lsh_globals(rows, edges, counts, kr, n_samples=32768, seed=42)
+            p2 = os.path.join(td, "legacy.graph")
+            D.write_legacy_directional(p2, rows, edges, edist, counts, medoid, 32, kr, packed, mag,
+                                       c, nd, pq["centroids"], pq["codes"], D.norms(rows))
+            with stdout_to_stderr():
+                h = getattr(mod, f"jasper_load_directional_{cfg}")(p2, 128, False, True, 4)
+        try:
+            flags = getattr(mod, f"jasper_get_directional_flags_{cfg}")(h)
+            for name in ("directional_search", "pq_search"):
+                fn = getattr(mod, f"jasper_{name}_{cfg}")
+                line = {"impl": "reference", "mode": "directional", "config": "config3",
+                        "estimator": "lsh" if name == "directional_search" else "pq",
+                        "k_ranks" if name == "directional_search" else "pq_m": kr,
+                        "flags": int(flags), "variant": variant}
+                oi = torch.empty(1000, K, dtype=torch.int32, device="cuda")
+                od = torch.empty(1000, K, dtype=torch.float32, device="cuda")
+                for bw in (64, 128):
+                    with stdout_to_stderr():
+                        fn(h, Qd, oi, od, K, bw, 2 * bw, False)
+                    torch.cuda.synchronize()
+                    r = recall_at_k(oi, gt)
+                    ts = []
+                    for it in range(args.warmup + args.steps):
+                        torch.cuda.synchronize()
+                        t1 = time.perf_counter()
+                        with stdout_to_stderr():
+                            fn(h, Qd, oi, od, K, bw, 2 * bw, False)
+                        torch.cuda.synchronize()
+                        if it >= args.warmup:
+                            ts.append(time.perf_counter() - t1)
+                    line[f"bw{bw}"] = {"recall_at_10": round(r, 4),
+                                       "qps": round(1000 / float(np.mean(ts)), 1)}
+                print(json.dumps(line), flush=True)
+        finally:
+            mod.jasper_free_graph(h)
 
 
 def main():
@@ -827,8 +1229,14 @@ def main():
     ap.add_argument("--nq", type=int, default=10_000)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-ndebug", action="store_true",
+                    help="--impl reference: use the -DNDEBUG build of the reference")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the parity check against the reference build (oracle/_ref)")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the config-5 range-sharded leg of the default run")
     ap.add_argument("--mode", default="replicas",
-                    choices=["replicas", "sharded", "rotation", "directional", "rabitq"],
+                    choices=["replicas", "sharded", "rotation", "directional", "rabitq", "config1"],
                     help="replicas: config 2 per GPU (default); sharded: config 5 range "
                          "shards; rotation: the prerotation GEMM alone; directional: "
                          "config 3 (LSH / PQ); rabitq: config 4")
@@ -847,6 +1255,8 @@ def main():
         run_directional(args)
     elif args.mode == "rabitq":
         run_rabitq(args)
+    elif args.mode == "config1":
+        run_config1(args)
     else:
         run_jasper(args)
 

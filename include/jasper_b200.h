@@ -309,6 +309,15 @@ int jb_graph_get_rabitq(int64_t handle, uint32_t* out_node_bytes, uint8_t* store
 int jb_merge_topk(const int32_t* shard_idx, const float* shard_dist, uint32_t n_shards,
                   uint64_t n_queries, uint32_t k, int32_t* out_idx, float* out_dist, void* stream);
 
+/* jb_merge_topk with shard s's lists starting shard_stride elements after
+ * shard s-1's (shard_stride >= n_queries * k): the layout of one gathered
+ * buffer [n_shards][2][n_queries][k] in which each shard sends its ids and
+ * distance bits together (shard_stride = 2 * n_queries * k).  No reference
+ * counterpart. */
+int jb_merge_topk_strided(const int32_t* shard_idx, const float* shard_dist, uint64_t shard_stride,
+                          uint32_t n_shards, uint64_t n_queries, uint32_t k, int32_t* out_idx,
+                          float* out_dist, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -636,8 +636,19 @@ int jb_merge_topk(const int32_t* shard_idx, const float* shard_dist, uint32_t n_
   return guarded([&] {
     if (n_queries == 0) return;
     if (!shard_idx || !shard_dist || !out_idx || !out_dist) throw std::invalid_argument("null argument");
-    jb::launch_merge_topk(shard_idx, shard_dist, n_shards, n_queries, k, out_idx, out_dist,
-                          static_cast<cudaStream_t>(stream));
+    jb::launch_merge_topk(shard_idx, shard_dist, n_shards, n_queries, k, n_queries * k, out_idx,
+                          out_dist, static_cast<cudaStream_t>(stream));
+  });
+}
+
+int jb_merge_topk_strided(const int32_t* shard_idx, const float* shard_dist, uint64_t shard_stride,
+                          uint32_t n_shards, uint64_t n_queries, uint32_t k, int32_t* out_idx,
+                          float* out_dist, void* stream) {
+  return guarded([&] {
+    if (n_queries == 0) return;
+    if (!shard_idx || !shard_dist || !out_idx || !out_dist) throw std::invalid_argument("null argument");
+    jb::launch_merge_topk(shard_idx, shard_dist, n_shards, n_queries, k, shard_stride, out_idx,
+                          out_dist, static_cast<cudaStream_t>(stream));
   });
 }
 

@@ -1,5 +1,8 @@
 // merge.cu -- k-way merge of per-shard top-k lists, one warp per query.
 //
+// Shard s's list for query q starts at s * shard_stride + q * k (stride
+// n_queries * k when the shards are stacked; larger when each shard's ids and
+// distances travel interleaved in one gathered buffer).
 // Each range shard returns its own top-k with global ids (shards own disjoint
 // id ranges, so no id repeats).  The warp loads the n_shards * k candidates
 // as (distance, id) keys, sorts them with a bitonic network in shared memory
@@ -16,7 +19,8 @@ constexpr int kMergeCap = 1024;
 
 __global__ void __launch_bounds__(128) merge_topk_kernel(const int32_t* sidx, const float* sdist,
                                                          uint32_t ns, uint64_t nq, uint32_t k,
-                                                         int32_t* oidx, float* odist) {
+                                                         uint64_t stride, int32_t* oidx,
+                                                         float* odist) {
   __shared__ uint64_t buf[4][kMergeCap];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   uint64_t* a = buf[wid];
@@ -25,7 +29,7 @@ __global__ void __launch_bounds__(128) merge_topk_kernel(const int32_t* sidx, co
     const int total = int(ns * k);
     for (int i = lane; i < total; i += 32) {
       const uint32_t s = uint32_t(i) / k, j = uint32_t(i) % k;
-      const size_t off = (size_t(s) * nq + q) * k + j;
+      const size_t off = size_t(s) * stride + q * k + j;
       const int32_t id = sidx[off];
       a[i] = id < 0 ? kKeyMax : make_pair_key(sdist[off], uint32_t(id));
     }
@@ -46,12 +50,15 @@ __global__ void __launch_bounds__(128) merge_topk_kernel(const int32_t* sidx, co
 }  // namespace
 
 void launch_merge_topk(const int32_t* sidx, const float* sdist, uint32_t ns, uint64_t nq,
-                       uint32_t k, int32_t* oidx, float* odist, cudaStream_t st) {
+                       uint32_t k, uint64_t shard_stride, int32_t* oidx, float* odist,
+                       cudaStream_t st) {
   if (ns == 0 || k == 0) throw std::invalid_argument("n_shards and k must be > 0");
+  if (shard_stride < nq * k) throw std::invalid_argument("shard stride must be >= n_queries * k");
   if (uint64_t(ns) * k > kMergeCap) throw std::invalid_argument("n_shards * k must be <= 1024");
   uint64_t blocks = (nq + 3) / 4;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  merge_topk_kernel<<<uint32_t(blocks), 128, 0, st>>>(sidx, sdist, ns, nq, k, oidx, odist);
+  merge_topk_kernel<<<uint32_t(blocks), 128, 0, st>>>(sidx, sdist, ns, nq, k, shard_stride, oidx,
+                                                              odist);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("merge launch: ") + cudaGetErrorString(e));
 }

@@ -41,42 +41,63 @@ def split_queries(n_queries: int, world: int, rank: int) -> slice:
     return slice(off, off + cnt)
 
 
+def _pack(local_idx: torch.Tensor, local_dist: torch.Tensor) -> torch.Tensor:
+    """[2, nq, k] int32: ids, then the distances' bit patterns."""
+    nq, k = local_idx.shape
+    packed = torch.empty(2, nq, k, dtype=torch.int32, device=local_idx.device)
+    packed[0].copy_(local_idx)
+    packed[1].copy_(local_dist.to(torch.float32).view(torch.int32))
+    return packed
+
+
 def gather_topk(local_idx: torch.Tensor, local_dist: torch.Tensor, root: int = 0,
-                group=None) -> tuple[torch.Tensor, torch.Tensor] | None:
-    """Gather every rank's [nq, k] top-k to ``root`` as [n_shards, nq, k]
-    tensors (rank order); other ranks get None."""
+                group=None, out: torch.Tensor | None = None
+                ) -> tuple[torch.Tensor, torch.Tensor] | None:
+    """Gather every rank's [nq, k] top-k to ``root`` with ONE collective:
+    each rank sends its ids and distance bits as one [2, nq, k] buffer into
+    ``root``'s [world, 2, nq, k] buffer (``out`` if given).  Returns
+    ``(ids, dists)`` as [world, nq, k] views of that buffer on ``root``
+    (shard stride 2 * nq * k, which ``merge_topk`` reads in place) and None
+    elsewhere."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    li = local_idx.contiguous()
-    ld = local_dist.contiguous()
+    packed = _pack(local_idx, local_dist)
     if rank == root:
-        gi = [torch.empty_like(li) for _ in range(world)]
-        gd = [torch.empty_like(ld) for _ in range(world)]
-        dist.gather(li, gi, dst=root, group=group)
-        dist.gather(ld, gd, dst=root, group=group)
-        return torch.stack(gi), torch.stack(gd)
-    dist.gather(li, None, dst=root, group=group)
-    dist.gather(ld, None, dst=root, group=group)
+        nq, k = local_idx.shape
+        if out is None or out.shape != (world, 2, nq, k):
+            out = torch.empty(world, 2, nq, k, dtype=torch.int32, device=packed.device)
+        dist.gather(packed, list(out.unbind(0)), dst=root, group=group)
+        return out[:, 0], out[:, 1].view(torch.float32)
+    dist.gather(packed, None, dst=root, group=group)
     return None
 
 
 def merge_topk(shard_idx: torch.Tensor, shard_dist: torch.Tensor,
                k: int | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     """Merge [n_shards, nq, k] per-shard top-k lists (CUDA tensors) into the
-    global [nq, k] by (distance, id) with jb_merge_topk."""
+    global [nq, k] by (distance, id) with jb_merge_topk_strided.  The shard
+    dimension may have any stride >= nq * k (the views ``gather_topk``
+    returns are read in place); the inner [nq, k] must be contiguous."""
     if not shard_idx.is_cuda or not shard_dist.is_cuda:
         raise ValueError("merge_topk needs CUDA tensors")
     ns, nq, kk = shard_idx.shape
     k = kk if k is None else k
-    si = shard_idx.to(torch.int32).contiguous()
-    sd = shard_dist.to(torch.float32).contiguous()
-    oi = torch.empty(nq, k, dtype=torch.int32, device=si.device)
-    od = torch.empty(nq, k, dtype=torch.float32, device=si.device)
     if k != kk:
         raise ValueError("k must equal the per-shard k")
-    _lib.call("jb_merge_topk", si.data_ptr(), sd.data_ptr(), ns, nq, k, oi.data_ptr(),
-              od.data_ptr(), torch.cuda.current_stream(si.device).cuda_stream)
+
+    def prep(t, dtype):
+        if t.dtype != dtype or t.stride(1) != kk or t.stride(2) != 1 or t.stride(0) < nq * kk:
+            t = t.to(dtype).contiguous()
+        return t
+    si = prep(shard_idx, torch.int32)
+    sd = prep(shard_dist, torch.float32)
+    if si.stride(0) != sd.stride(0):
+        si, sd = si.contiguous(), sd.contiguous()
+    oi = torch.empty(nq, k, dtype=torch.int32, device=si.device)
+    od = torch.empty(nq, k, dtype=torch.float32, device=si.device)
+    _lib.call("jb_merge_topk_strided", si.data_ptr(), sd.data_ptr(), si.stride(0), ns, nq, k,
+              oi.data_ptr(), od.data_ptr(), torch.cuda.current_stream(si.device).cuda_stream)
     return oi, od
 
 
@@ -88,6 +109,7 @@ class ShardedGraph:
         self.offset = offset
         self.n_total = n_total
         self.group = group
+        self._gather_buf = None   # root's [world, 2, nq, k] gather buffer, reused
 
     @classmethod
     def build(cls, local_vectors: torch.Tensor, offset: int, n_total: int, group=None,
@@ -102,14 +124,31 @@ class ShardedGraph:
         """This shard's top-k (global ids) for all queries."""
         return self.graph.search(queries, k=k, beam_width=beam_width)
 
-    def search(self, queries: torch.Tensor, k: int = 10, beam_width: int = 64, root: int = 0):
+    def search(self, queries: torch.Tensor, k: int = 10, beam_width: int = 64, root: int = 0,
+               phases: list | None = None):
         """All ranks call this with the same queries.  Returns the merged
-        global top-k on ``root`` and None elsewhere."""
+        global top-k on ``root`` and None elsewhere.  With ``phases`` (a
+        list), appends CUDA events (start, searched, gathered, merged) on the
+        current stream, for per-phase timing."""
+        ev = None
+        if phases is not None:
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record()
         li, ld = self.search_local(queries, k, beam_width)
-        g = gather_topk(li, ld, root=root, group=self.group)
+        if ev is not None:
+            ev[1].record()
+        g = gather_topk(li, ld, root=root, group=self.group, out=self._gather_buf)
+        if ev is not None:
+            ev[2].record()
         if g is None:
-            return None
-        return merge_topk(g[0], g[1], k)
+            out = None
+        else:
+            self._gather_buf = g[0]._base if g[0]._base is not None else None
+            out = merge_topk(g[0], g[1], k)
+        if ev is not None:
+            ev[3].record()
+            phases.append(ev)
+        return out
 
     def free(self):
         self.graph.free()

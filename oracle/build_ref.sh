@@ -37,6 +37,17 @@ g++ -shared -o "$OUT/lib/libjasper_ffi.so" $objs "$OUT/obj/dlink.o" \
   -L/usr/local/cuda/lib64 -lcudart -lcublas -lcurand \
   -L$TVM/lib -ltvm_ffi -Wl,-rpath,$TVM/lib -Wl,-rpath,/usr/local/cuda/lib64
 echo "built $OUT/lib/libjasper_ffi.so"
+# The same plain-graph ops built with -DNDEBUG (device asserts compiled out):
+# a second, stricter reference bar for the benchmark (bench.py --ref-ndebug).
+NDOBJ=$OUT/obj/plain_ndebug.o
+if [ ! -f "$NDOBJ" ] || [ "$REF/ffi/jasper_ffi_plain.cu" -nt "$NDOBJ" ]; then
+  nvcc $FLAGS -DNDEBUG -c "$REF/ffi/jasper_ffi_plain.cu" -o "$NDOBJ" > "$OUT/obj/plain_ndebug.log" 2>&1
+fi
+nvcc -gencode arch=compute_100a,code=sm_100a -dlink -Xcompiler -fPIC "$NDOBJ" -o "$OUT/obj/dlink_ndebug.o"
+g++ -shared -o "$OUT/lib/libjasper_ffi_ndebug.so" "$NDOBJ" "$OUT/obj/dlink_ndebug.o" \
+  -L/usr/local/cuda/lib64 -lcudart -lcublas -lcurand \
+  -L$TVM/lib -ltvm_ffi -Wl,-rpath,$TVM/lib -Wl,-rpath,/usr/local/cuda/lib64
+echo "built $OUT/lib/libjasper_ffi_ndebug.so"
 # RaBitQ quantizer driver (header-only reference code; our main() in
 # oracle/ref_rabitq_driver.cu)
 mkdir -p "$OUT/bin"

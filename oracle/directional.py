@@ -177,3 +177,44 @@ def write_legacy_directional(path, X, edges, edist, counts, medoid, R, k_ranks, 
         out += np.asarray(nrm, np.float32).tobytes()
     with open(path, "wb") as f:
         f.write(bytes(out))
+
+
+def read_directional_file(path, dim, R):
+    """Reads a graph file with the full base layout (records with ids,
+    deletion bitmask, next_id; graph.cuh:1653-1788) and, if present, the
+    directional trailer behind it (graph.cuh:1814-1937).  Returns (rows
+    [n, dim] fp16, edges [n, R] u32, bf16 edge distances [n, R] u16, counts
+    [n] u8, medoid, pq) with pq = {"centroids": [M, K, dsub] f32, "codes":
+    [n, R*M] u8} or None."""
+    raw = open(path, "rb").read()
+    _, n, medoid, bpn = struct.unpack_from("<4Q", raw, 0)
+    if bpn != 2 * dim + 1 + 6 * R + 4:
+        raise ValueError(f"bytes_per_node {bpn} is not the full layout for dim={dim}, R={R}")
+    rec = np.frombuffer(raw, np.uint8, count=n * bpn, offset=32).reshape(n, bpn)
+    rows = rec[:, :2 * dim].copy().view(np.float16)
+    counts = rec[:, 2 * dim].copy()
+    o = 2 * dim + 1
+    edges = rec[:, o:o + 4 * R].copy().view(np.uint32)
+    edist = rec[:, o + 4 * R:o + 6 * R].copy().view(np.uint16)
+    off = 32 + n * bpn + (n + 7) // 8 + 8
+    pq = None
+    if off + 9 <= len(raw):
+        magic, version, flags = struct.unpack_from("<IIB", raw, off)
+        if magic == 0x484C5344:
+            off += 9
+            if flags & 1:
+                kr, ps = struct.unpack_from("<BB", raw, off)
+                off += 2 + 4 * kr + 4
+                r = R * kr * ps + 2 * R
+                off += n * ((r + 3) // 4 * 4)
+            if flags & 2:
+                M, Kc, dsub = struct.unpack_from("<III", raw, off)
+                off += 12
+                cent = np.frombuffer(raw, np.float32, count=M * Kc * dsub,
+                                     offset=off).reshape(M, Kc, dsub).copy()
+                off += 4 * M * Kc * dsub
+                r = R * M
+                rp = (r + 3) // 4 * 4
+                codes = np.frombuffer(raw, np.uint8, count=n * rp, offset=off).reshape(n, rp)
+                pq = {"centroids": cent, "codes": codes[:, :r].copy()}
+    return rows, edges, edist, counts, int(medoid), pq
