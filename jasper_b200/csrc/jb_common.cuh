@@ -44,6 +44,11 @@ __device__ __forceinline__ uint64_t make_pair_key(float d, uint32_t id) {
 __device__ __forceinline__ uint32_t pair_id(uint64_t k) { return uint32_t(k); }
 
 // Read-only 16-byte gather through the non-coherent path.
+// Hint: bring the 128-byte line holding p into L2 (no register, no wait).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 __device__ __forceinline__ uint4 ldg16(const uint4* p) {
   uint4 r;
   asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"

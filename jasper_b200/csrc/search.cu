@@ -34,8 +34,11 @@
 // Loop bounds follow beam_search.cuh:129-203: at most limit + 1 rounds; a
 // round expands the first unvisited beam entry; when the expansion count
 // reaches max_result_size the loop stops before adding that node's neighbours.
+#include <map>
+#include <mutex>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include "jb_common.cuh"
 #include "search.cuh"
 
@@ -436,6 +439,20 @@ __device__ __forceinline__ float warp_sum_xor(float v) {
   return v;
 }
 
+// L2 prefetch hints (bit 0: rows of new candidates; bit 1: the neighbour
+// list of every candidate that enters the beam, read when it is expanded).
+#ifndef JB_PREFETCH
+#define JB_PREFETCH 0
+#endif
+constexpr int kPrefetch = JB_PREFETCH;
+
+__device__ __forceinline__ void prefetch_edges(const GraphView& g, uint32_t id) {
+  const uint32_t l = id - g.global_offset;
+  const char* e = reinterpret_cast<const char*>(g.edges + size_t(l) * g.R);
+  for (uint32_t o = 0; o < 4 * g.R; o += 128) prefetch_l2(e + o);
+  prefetch_l2(g.counts + l);
+}
+
 #ifndef JB_SEARCH_MIN_BLOCKS
 #define JB_SEARCH_MIN_BLOCKS 4
 #endif
@@ -447,14 +464,22 @@ constexpr int kCountMerge = JB_COUNT_MERGE;
 #ifndef JB_TILE_MIN_BLOCKS
 #define JB_TILE_MIN_BLOCKS 6
 #endif
-// The tile path fits in 80 registers; shared memory then allows 5 CTAs per SM.
-template <int MAXC, int METRIC>
+#ifndef JB_TILE_MIN_BLOCKS_B32
+#define JB_TILE_MIN_BLOCKS_B32 8
+#endif
+// The tile path fits in 80 registers; with a 2^11-slot visited table shared
+// memory then allows 5 CTAs per SM.  Beams of at most 32 use a 2^10-slot
+// table (6.4 KB per query), so 8 CTAs fit in shared memory and the kernel is
+// compiled for 8 (64 registers): 32 queries in flight per SM instead of 20.
+template <int MAXC, int METRIC, uint32_t BWCAP>
 constexpr int search_min_blocks() {
-  return (MAXC > 0 && MAXC <= 4 && METRIC == kL2) ? JB_TILE_MIN_BLOCKS : JB_SEARCH_MIN_BLOCKS;
+  return (MAXC > 0 && MAXC <= 4 && METRIC == kL2)
+             ? (BWCAP <= 32 ? JB_TILE_MIN_BLOCKS_B32 : JB_TILE_MIN_BLOCKS)
+             : JB_SEARCH_MIN_BLOCKS;
 }
 
 template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC>
-__global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC>())
+__global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC, BWCAP>())
     beam_search_warp_kernel(SearchArgs a) {
   constexpr bool kRegQ = (MAXC > 0);
 #ifndef JB_NO_TILE4
@@ -742,6 +767,18 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC>())
       const uint32_t lt = (1u << lane) - 1u;
       if (f0) sm.cand_ids[__popc(b0 & lt)] = nb0;
       if (f1) sm.cand_ids[__popc(b0) + __popc(b1 & lt)] = nb1;
+      if constexpr ((kPrefetch & 1) != 0) {
+        // the rows of every new candidate: the later distance rounds find
+        // them in L2 while the first round's loads are still in flight
+        if (f0 || f1) {
+          const char* r0 = reinterpret_cast<const char*>(g.vec + size_t(nb0 - g.global_offset) * dpad);
+          const char* r1 = reinterpret_cast<const char*>(g.vec + size_t(nb1 - g.global_offset) * dpad);
+          for (uint32_t o = 0; o < 2 * dpad; o += 128) {
+            if (f0) prefetch_l2(r0 + o);
+            if (f1) prefetch_l2(r1 + o);
+          }
+        }
+      }
       int m = __popc(b0) + __popc(b1);
       n_hash += m;
       __syncwarp();
@@ -793,7 +830,10 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC>())
           uint32_t r = 0;
           for (int j = 0; j < kept; j++) r += sm.cand_keys[j] < c;
           const uint32_t p = r + lower_rank(cur, int(cnt), c);
-          if (p < bw) nxt[p] = c;
+          if (p < bw) {
+            nxt[p] = c;
+            if constexpr ((kPrefetch & 2) != 0) prefetch_edges(g, key_id(c));
+          }
         }
       } else {
         for (uint32_t i = lane; i < cnt; i += 32) {
@@ -804,7 +844,10 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC>())
         for (int j = lane; j < kept; j += 32) {
           const uint64_t c = sm.cand_keys[j];
           const uint32_t p = j + lower_rank(cur, int(cnt), c);
-          if (p < bw) nxt[p] = c;
+          if (p < bw) {
+            nxt[p] = c;
+            if constexpr ((kPrefetch & 2) != 0) prefetch_edges(g, key_id(c));
+          }
         }
       }
       cnt = min(bw, cnt + uint32_t(kept));
@@ -869,12 +912,30 @@ void launch_t(const SearchArgs& a, cudaStream_t stream) {
   while (wpb > 1 && per_warp * wpb > 200 * 1024) wpb--;
   if (per_warp * wpb > 220 * 1024) throw std::runtime_error("search: shared memory per query too large");
   const size_t smem = per_warp * wpb;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-  int dev = 0, sms = 0, per_sm = 0;
+  // The shared-memory opt-in and the occupancy query cost a few microseconds
+  // each; they depend only on (instantiation, device, shared memory), so they
+  // run once per such triple.
+  struct Launch { size_t smem; int sms, per_sm; };
+  static std::mutex m;
+  static std::map<std::pair<int, size_t>, Launch> cache;
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 32 * wpb, smem);
-  if (per_sm < 1) per_sm = 1;
+  Launch L{};
+  {
+    std::lock_guard<std::mutex> lock(m);
+    auto it = cache.find({dev, smem});
+    if (it != cache.end()) {
+      L = it->second;
+    } else {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      L.smem = smem;
+      cudaDeviceGetAttribute(&L.sms, cudaDevAttrMultiProcessorCount, dev);
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&L.per_sm, kern, 32 * wpb, smem);
+      if (L.per_sm < 1) L.per_sm = 1;
+      cache[{dev, smem}] = L;
+    }
+  }
+  const int sms = L.sms, per_sm = L.per_sm;
   const uint32_t need = (a.nq + wpb - 1) / wpb;
   uint32_t grid = uint32_t(sms) * uint32_t(per_sm);
   if (grid > need) grid = need;
@@ -927,6 +988,10 @@ void launch_search(const SearchArgs& a, cudaStream_t stream) {
 #ifndef JB_HBITS64
 #define JB_HBITS64 11
 #endif
+#ifndef JB_HBITS32
+#define JB_HBITS32 10
+#endif
+  if (a.bw <= 32) return dispatch_dim<32, JB_HBITS32>(a, stream);
   if (a.bw <= 64) return dispatch_dim<64, JB_HBITS64>(a, stream);
   if (a.bw <= 128) return dispatch_dim<128, 11>(a, stream);
   if (a.bw <= 256) return dispatch_dim<256, 11>(a, stream);
