@@ -18,7 +18,7 @@
 //    that is still in the beam is dropped by the reference's stable dedup
 //    (the beam copy comes first and keeps its visited bit), and one that was
 //    clipped before has at least beam_width strictly smaller entries ahead of
-//    it and is clipped again.  When the table passes half full it is cleared
+//    it and is clipped again.  When the table passes 5/8 full it is cleared
 //    and refilled with the current beam, so beam members are always found;
 //    forgotten clipped ids are merely recomputed, and clipped again;
 //  * out-of-range neighbours (the global_offset range test of
@@ -46,6 +46,13 @@ namespace jb {
 namespace {
 
 constexpr uint32_t kHashEmpty = 0xFFFFFFFFu;
+// The visited table is cleared (and refilled with the beam) before an
+// expansion could take it past kHashFillNum / kHashFillDen of its slots.
+#ifndef JB_HASH_FILL_NUM
+#define JB_HASH_FILL_NUM 5
+#define JB_HASH_FILL_DEN 8
+#endif
+constexpr uint32_t kHashFillNum = JB_HASH_FILL_NUM, kHashFillDen = JB_HASH_FILL_DEN;
 
 // Optional per-phase cycle counters (build with -DJB_PHASE_CLOCKS; read with
 // jb_debug_phase_clocks): 0 init, 1 choose, 2 neighbour list + filter,
@@ -105,7 +112,7 @@ __device__ __forceinline__ WarpSmem carve(char* base, uint32_t bwcap, uint32_t h
 }
 
 // Insert id; true when it was absent.  The caller keeps the table at most
-// half full, so the probe sequence always ends at an empty slot.
+// below 5/8 full, so the probe sequence always ends at an empty slot.
 __device__ __forceinline__ bool hash_insert(uint32_t* h, uint32_t hbits, uint32_t id) {
   const uint32_t mask = (1u << hbits) - 1u;
   uint32_t slot = (id * 0x9E3779B1u) >> (32 - hbits);
@@ -738,9 +745,9 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC, BWCAP>())
       expansions++;
       if (expansions == a.max_result_size) break;
 
-      // Keep the visited-distance table at most half full: clear it and refill
+      // Keep the visited-distance table at most 5/8 full: clear it and refill
       // it with the beam, so beam members are always recognised.
-      if (n_hash + R > hsize / 2) {
+      if (n_hash + R > kHashFillNum * (hsize / kHashFillDen)) {
         __syncwarp();
         for (uint32_t i = lane; i < hsize; i += 32) sm.hash[i] = kHashEmpty;
         __syncwarp();
@@ -913,22 +920,27 @@ void launch_t(const SearchArgs& a, cudaStream_t stream) {
   if (per_warp * wpb > 220 * 1024) throw std::runtime_error("search: shared memory per query too large");
   const size_t smem = per_warp * wpb;
   // The shared-memory opt-in and the occupancy query cost a few microseconds
-  // each; they depend only on (instantiation, device, shared memory), so they
-  // run once per such triple.
-  struct Launch { size_t smem; int sms, per_sm; };
+  // each, so they are cached per (instantiation, device).  The opt-in is a
+  // maximum: it is only ever raised, never lowered by a smaller launch, so a
+  // cached larger launch stays valid.
+  struct Launch { int sms, per_sm; };
   static std::mutex m;
   static std::map<std::pair<int, size_t>, Launch> cache;
+  static std::map<int, size_t> opted;
   int dev = 0;
   cudaGetDevice(&dev);
   Launch L{};
   {
     std::lock_guard<std::mutex> lock(m);
+    size_t& cur = opted[dev];
+    if (smem > cur) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      cur = smem;
+    }
     auto it = cache.find({dev, smem});
     if (it != cache.end()) {
       L = it->second;
     } else {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-      L.smem = smem;
       cudaDeviceGetAttribute(&L.sms, cudaDevAttrMultiProcessorCount, dev);
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&L.per_sm, kern, 32 * wpb, smem);
       if (L.per_sm < 1) L.per_sm = 1;
