@@ -111,8 +111,8 @@ __device__ __forceinline__ WarpSmem carve(char* base, uint32_t bwcap, uint32_t h
   return s;
 }
 
-// Insert id; true when it was absent.  The caller keeps the table at most
-// below 5/8 full, so the probe sequence always ends at an empty slot.
+// Insert id; true when it was absent.  The caller keeps the table below
+// 5/8 full, so the probe sequence always ends at an empty slot.
 __device__ __forceinline__ bool hash_insert(uint32_t* h, uint32_t hbits, uint32_t id) {
   const uint32_t mask = (1u << hbits) - 1u;
   uint32_t slot = (id * 0x9E3779B1u) >> (32 - hbits);
