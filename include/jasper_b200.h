@@ -143,6 +143,18 @@ int jb_graph_reserve_ids(int64_t handle, int64_t count, int32_t* out_ids);
  * include/jasper/index/graph_ops.cuh:93-134). */
 int jb_graph_mark_deleted(int64_t handle, const int32_t* ids, uint64_t n_ids);
 
+/* Live append (reference: Append_##id, ffi/jasper_ffi_common.cuh:411-432 ->
+ * jasper::append_batch, include/jasper/index/construct.cuh:1169-1265): the
+ * n rows (host or device memory, row stride `row_stride` elements) take the
+ * next slots, are wired into the graph by the construction's batched search
+ * and RobustPrune(alpha) in batches of min(n, 100000) rows, and receive the
+ * stable ids next_id .. next_id + n - 1, written to the host int32 array
+ * `out_ids` (may be NULL).  Device-resident plain graphs with global offset 0
+ * only (directional, RaBitQ or prerotated graphs are rejected, as the
+ * reference exports no directional append).  Synchronous on `stream`. */
+int jb_graph_append(int64_t handle, const uint16_t* vectors, uint64_t n, uint32_t row_stride,
+                    double alpha, int32_t* out_ids, void* stream);
+
 /* Create a graph from rows with no edges (host or device rows). */
 int jb_graph_create(const uint16_t* vectors, uint64_t n, uint32_t dim, uint32_t row_stride,
                     uint32_t n_neighbors, int32_t metric, int32_t on_host, int64_t* out_handle);

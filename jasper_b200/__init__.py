@@ -403,7 +403,24 @@ class Graph:
         _lib.call("jb_graph_mark_deleted", self._handle, _ptr(ids), ids.numel())
 
     def append(self, vectors: torch.Tensor, alpha: float = 1.2) -> torch.Tensor:
-        raise NotImplementedError("append() is not part of this build")
+        """Append a batch of vectors to the live graph (python/jasper/
+        __init__.py:673-697): the new rows are wired in with the
+        construction's batched beam search + RobustPrune(alpha) and get
+        fresh monotonic stable ids.  Returns the ids (int32, CPU) in input
+        order."""
+        self._check_alive()
+        if not vectors.is_cuda:
+            raise ValueError("vectors must be a CUDA tensor")
+        if vectors.dtype != torch.float16:
+            raise ValueError(f"vectors must be torch.float16, got {vectors.dtype}")
+        if vectors.ndim != 2 or vectors.size(1) != self.dim:
+            raise ValueError(f"vectors must be [n, {self.dim}]")
+        vectors = vectors.contiguous()
+        n = vectors.size(0)
+        out_ids = torch.empty(n, dtype=torch.int32)
+        _lib.call("jb_graph_append", self._handle, _ptr(vectors), n, vectors.size(1),
+                  float(alpha), _ptr(out_ids), _stream_ptr(vectors.device))
+        return out_ids
 
     def consolidate(self, alpha: float = 1.2) -> None:
         raise NotImplementedError("consolidate() is not part of this build")

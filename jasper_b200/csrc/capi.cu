@@ -437,6 +437,19 @@ int jb_graph_mark_deleted(int64_t handle, const int32_t* ids, uint64_t n_ids) {
   });
 }
 
+int jb_graph_append(int64_t handle, const uint16_t* vectors, uint64_t n, uint32_t row_stride,
+                    double alpha, int32_t* out_ids, void* stream) {
+  return guarded([&] {
+    auto g = lookup(handle);
+    DeviceScope ds(g->device);
+    if (n > 0 && vectors == nullptr) throw std::invalid_argument("vectors is null");
+    auto ids = jb::graph_append(*g, vectors, n, row_stride, float(alpha),
+                                static_cast<cudaStream_t>(stream));
+    if (out_ids != nullptr)
+      for (size_t i = 0; i < ids.size(); i++) out_ids[i] = int32_t(ids[i]);
+  });
+}
+
 int jb_graph_set_edges(int64_t handle, const uint32_t* edges, const uint16_t* edge_dists,
                        const uint8_t* counts, uint32_t medoid) {
   return guarded([&] {

@@ -33,6 +33,7 @@
 // that, deterministically: existing edges, then sinks in (target, sink) order
 // until the cap; the sinks past the cap are never evaluated.
 #include <cub/device/device_radix_sort.cuh>
+#include <algorithm>
 #include <cstdlib>
 #include <stdexcept>
 #include <string>
@@ -929,6 +930,63 @@ void process_batch(Graph& graph, BuildWorkspace& ws, uint32_t off, uint32_t bs, 
   if (g.metric == kIP) dispatch_prune<kIP>(g, off, bs, ws, alpha, st, true, total);
   else dispatch_prune<kL2>(g, off, bs, ws, alpha, st, true, total);
   check(cudaGetLastError(), "construct batch launch");
+}
+
+// append_batch (include/jasper/index/construct.cuh:1169-1265): the new rows
+// take slots [n, n + count), their edges are wired by process_batch in
+// batches of min(count, 100000) rows -- no ramp -- and they get the stable
+// ids next_id, next_id + 1, ...  Arrays grow geometrically (1.5x), so a
+// sequence of appends costs amortised O(rows appended) in copies.
+std::vector<uint32_t> graph_append(Graph& graph, const uint16_t* rows, uint64_t count,
+                                   uint32_t stride, float alpha, cudaStream_t st) {
+  std::vector<uint32_t> ids;
+  if (count == 0) return ids;
+  if (graph.on_host) throw std::runtime_error("append requires a device-resident graph");
+  if (graph.global_offset != 0) throw std::runtime_error("append requires global_offset == 0");
+  if (graph.dir.has_lsh || graph.dir.has_pq || graph.dir.has_rabitq || graph.dir.prerotate)
+    throw std::runtime_error("append is for plain graphs (the graph has directional, RaBitQ or "
+                             "prerotation artifacts)");
+  if (stride < graph.dim) throw std::invalid_argument("row stride is smaller than dim");
+  const uint64_t old_n = graph.n, new_n = old_n + count;
+  if (new_n >= 0x7FFFFFFFull) throw std::invalid_argument("graphs are limited to 2^31 - 1 rows");
+  if (graph.next_id + count > 0xFFFFFFFFull) throw std::runtime_error("stable ids exhausted");
+  if (new_n > graph.capacity) {
+    const uint64_t grown = uint64_t(graph.capacity) + graph.capacity / 2;
+    graph_reserve(graph, uint32_t(std::min<uint64_t>(std::max(new_n, grown), 0x7FFFFFFEull)));
+  }
+  const size_t dp = graph.dpad;
+  uint16_t* dst = graph.vec + old_n * dp;
+  if (dp != graph.dim) check(cudaMemsetAsync(dst, 0, count * dp * 2, st), "clear appended rows");
+  check(cudaMemcpy2DAsync(dst, dp * 2, rows, size_t(stride) * 2, size_t(graph.dim) * 2, count,
+                          cudaMemcpyDefault, st),
+        "copy appended rows");
+  check(cudaMemsetAsync(graph.counts + old_n, 0, count, st), "clear appended counts");
+  ids.resize(count);
+  for (uint64_t i = 0; i < count; i++) ids[i] = uint32_t(graph.next_id + i);
+  check(cudaMemcpyAsync(graph.slot_to_id + old_n, ids.data(), count * 4, cudaMemcpyHostToDevice,
+                        st),
+        "write appended ids");
+  check(cudaStreamSynchronize(st), "append upload");
+  if (graph.next_id != old_n) graph.ids_identity = false;
+  graph.n = uint32_t(new_n);
+  graph.next_id += count;
+  const uint32_t max_batch = uint32_t(std::min<uint64_t>(count, 100000));
+  BuildWorkspace ws;
+  workspace_allocate(ws, max_batch, graph.R);
+  try {
+    for (uint64_t off = old_n; off < new_n;) {
+      const uint32_t bs = uint32_t(std::min<uint64_t>(max_batch, new_n - off));
+      process_batch(graph, ws, uint32_t(off), bs, alpha, st);
+      off += bs;
+    }
+    check(cudaStreamSynchronize(st), "append");
+  } catch (...) {
+    cudaStreamSynchronize(st);
+    workspace_free(ws);
+    throw;
+  }
+  workspace_free(ws);
+  return ids;
 }
 
 void construct_graph(Graph& graph, float alpha, uint32_t max_batch, cudaStream_t st) {

@@ -1,6 +1,7 @@
 // construct.cuh -- batched Vamana construction driver.
 #pragma once
 #include <cuda_runtime.h>
+#include <vector>
 #include "jb_graph.h"
 
 namespace jb {
@@ -33,6 +34,11 @@ void workspace_free(BuildWorkspace& ws);
 // One batch: rows [off, off + bs) (global ids), stream-ordered.
 void process_batch(Graph& g, BuildWorkspace& ws, uint32_t off, uint32_t bs, float alpha,
                    cudaStream_t stream);
+
+// Live append of `count` rows (host or device, row stride `stride` elements):
+// returns their stable ids.  Synchronises `stream`.
+std::vector<uint32_t> graph_append(Graph& g, const uint16_t* rows, uint64_t count,
+                                   uint32_t stride, float alpha, cudaStream_t stream);
 
 // Whole build over the rows already uploaded to g (edge counts zero).
 void construct_graph(Graph& g, float alpha, uint32_t max_batch, cudaStream_t stream);

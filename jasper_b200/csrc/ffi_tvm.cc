@@ -23,7 +23,9 @@
 #include <tvm/ffi/extra/c_env_api.h>
 #include <tvm/ffi/tvm_ffi.h>
 
+#include <cuda_runtime.h>
 #include <string>
+#include <vector>
 
 #include "jasper_b200.h"
 
@@ -89,8 +91,15 @@ struct Ops {
     TVM_FFI_THROW(RuntimeError) << "consolidate is not part of jasper_b200";
   }
   static void Compact(int64_t) { TVM_FFI_THROW(RuntimeError) << "compact is not part of jasper_b200"; }
-  static void Append(int64_t, ffi::TensorView, double, ffi::TensorView) {
-    TVM_FFI_THROW(RuntimeError) << "append is not part of jasper_b200";
+  // out_ids: host int32 [n] (the reference copies its ids there with
+  // cudaMemcpyDefault, ffi/jasper_ffi_common.cuh:428-431).
+  static void Append(int64_t handle, ffi::TensorView vectors, double alpha,
+                     ffi::TensorView out_ids) {
+    const uint64_t n = uint64_t(vectors.size(0));
+    std::vector<int32_t> ids(n);
+    check(jb_graph_append(handle, static_cast<const uint16_t*>(vectors.data_ptr()), n,
+                          row_stride(vectors), alpha, ids.data(), stream_of(vectors)));
+    if (n > 0) cudaMemcpy(out_ids.data_ptr(), ids.data(), n * 4, cudaMemcpyDefault);
   }
 };
 

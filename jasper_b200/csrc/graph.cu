@@ -60,6 +60,7 @@ void graph_allocate(Graph& g, uint32_t dim, uint32_t R, int metric, uint32_t n, 
   g.R = R;
   g.metric = metric;
   g.n = n;
+  g.capacity = n;
   g.on_host = on_host;
   g.next_id = n;
   try {
@@ -84,6 +85,44 @@ void graph_allocate(Graph& g, uint32_t dim, uint32_t R, int metric, uint32_t n, 
     graph_free(g);
     throw;
   }
+}
+
+void graph_reserve(Graph& g, uint32_t rows) {
+  if (rows <= g.capacity) return;
+  if (g.on_host) throw std::runtime_error("graph_reserve: graph rows live in host memory");
+  if (rows >= 0x7FFFFFFFu) throw std::invalid_argument("graphs are limited to 2^31 - 1 rows");
+  const size_t n = g.n, R = g.R, dp = g.dpad;
+  const size_t wn = (n + 31) / 32, wc = (size_t(rows) + 31) / 32;
+  uint16_t* vec = nullptr; uint32_t* edges = nullptr; uint16_t* edist = nullptr;
+  uint8_t* counts = nullptr; uint32_t* ids = nullptr; uint32_t* del = nullptr;
+  try {
+    vec = alloc_array<uint16_t>(size_t(rows) * dp, false, "grow vectors");
+    edges = alloc_array<uint32_t>(size_t(rows) * R, false, "grow edges");
+    edist = alloc_array<uint16_t>(size_t(rows) * R, false, "grow edge distances");
+    counts = alloc_array<uint8_t>(rows, false, "grow edge counts");
+    ids = alloc_array<uint32_t>(rows, false, "grow slot ids");
+    del = alloc_array<uint32_t>(wc, false, "grow deletion bits");
+    check(cudaMemcpy(vec, g.vec, n * dp * 2, cudaMemcpyDeviceToDevice), "grow copy");
+    check(cudaMemcpy(edges, g.edges, n * R * 4, cudaMemcpyDeviceToDevice), "grow copy");
+    check(cudaMemset(edges + n * R, 0xFF, (rows - n) * R * 4), "grow memset");
+    check(cudaMemcpy(edist, g.edist, n * R * 2, cudaMemcpyDeviceToDevice), "grow copy");
+    check(cudaMemset(edist + n * R, 0, (rows - n) * R * 2), "grow memset");
+    check(cudaMemcpy(counts, g.counts, n, cudaMemcpyDeviceToDevice), "grow copy");
+    check(cudaMemset(counts + n, 0, rows - n), "grow memset");
+    check(cudaMemcpy(ids, g.slot_to_id, n * 4, cudaMemcpyDeviceToDevice), "grow copy");
+    check(cudaMemset(del, 0, wc * 4), "grow memset");
+    check(cudaMemcpy(del, g.deleted, wn * 4, cudaMemcpyDeviceToDevice), "grow copy");
+  } catch (...) {
+    for (void* p : {static_cast<void*>(vec), static_cast<void*>(edges), static_cast<void*>(edist),
+                    static_cast<void*>(counts), static_cast<void*>(ids), static_cast<void*>(del)})
+      free_array(p, false);
+    throw;
+  }
+  free_array(g.vec, false); free_array(g.edges, false); free_array(g.edist, false);
+  free_array(g.counts, false); free_array(g.slot_to_id, false); free_array(g.deleted, false);
+  g.vec = vec; g.edges = edges; g.edist = edist; g.counts = counts; g.slot_to_id = ids;
+  g.deleted = del;
+  g.capacity = rows;
 }
 
 void graph_free_directional(Graph& g) {
@@ -112,6 +151,7 @@ void graph_free(Graph& g) {
   g.vec = nullptr; g.edges = nullptr; g.edist = nullptr; g.counts = nullptr;
   g.slot_to_id = nullptr; g.deleted = nullptr;
   g.n = 0;
+  g.capacity = 0;
 }
 
 void graph_upload_rows(Graph& g, const uint16_t* rows, uint32_t stride) {

@@ -71,6 +71,7 @@ struct Graph {
   uint32_t dim = 0, dpad = 0, R = 0;
   int metric = kL2;
   uint32_t n = 0;
+  uint32_t capacity = 0;       // rows the arrays hold (>= n; grows on append)
   uint32_t medoid = 0;
   uint32_t global_offset = 0;
   bool on_host = false;        // rows live in mapped pinned host memory
@@ -97,6 +98,9 @@ inline uint32_t pad_dim(uint32_t d) { return (d + 7u) / 8u * 8u; }
 // Host-side graph lifecycle (graph.cu).  All throw std::runtime_error.
 void graph_allocate(Graph& g, uint32_t dim, uint32_t R, int metric, uint32_t n, bool on_host);
 void graph_free(Graph& g);
+// Device-resident graphs: grow every per-row array to hold `rows` rows (the
+// first n rows kept; new edge counts and deletion bits zero).
+void graph_reserve(Graph& g, uint32_t rows);
 // Copy [n][dim] fp16 rows with row stride `stride` elements (host or device
 // pointer) into the padded row array.
 void graph_upload_rows(Graph& g, const uint16_t* rows, uint32_t stride);

@@ -575,6 +575,28 @@ void orc_build(orc_graph *g, float alpha, uint32_t max_batch_size) {
   free(vis_cnt);
 }
 
+/* Live append (append_batch, include/jasper/index/construct.cuh:1169-1265):
+ * rows [start, start + count) already sit in g with zero edge counts; they
+ * are wired in batches of max_batch rows starting at `start` -- no ramp,
+ * unlike the build (construct.cuh:1229-1240) -- with the construction's own
+ * process_batch. */
+void orc_append_range(orc_graph *g, uint32_t start, uint32_t count, float alpha,
+                      uint32_t max_batch) {
+  if (count == 0) return;
+  if (max_batch == 0) max_batch = count < 100000 ? count : 100000;
+  uint32_t *vis_idx = (uint32_t *)malloc(sizeof(uint32_t) * (size_t)max_batch * ORC_BUILD_MAX_RESULT);
+  float *vis_dist = (float *)malloc(sizeof(float) * (size_t)max_batch * ORC_BUILD_MAX_RESULT);
+  uint32_t *vis_cnt = (uint32_t *)malloc(sizeof(uint32_t) * max_batch);
+  for (uint32_t off = start; off < start + count;) {
+    uint32_t bs = start + count - off < max_batch ? start + count - off : max_batch;
+    process_batch(g, off, bs, alpha, vis_idx, vis_dist, vis_cnt);
+    off += bs;
+  }
+  free(vis_idx);
+  free(vis_dist);
+  free(vis_cnt);
+}
+
 /* ----------------------------------------------------- exact brute force */
 
 /* Multi-threaded exact kNN over fp16 rows (the CPU baseline named by the

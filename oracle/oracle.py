@@ -118,6 +118,32 @@ class OracleGraph:
         g = self._struct()
         lib().orc_build(C.byref(g), float(alpha), int(max_batch_size))
 
+    def append(self, vectors: np.ndarray, alpha: float, max_batch: int = 0) -> np.ndarray:
+        """Live append (orc_append_range): the rows join at slots [n, n + m)
+        and are wired in batches of min(m, 100000) rows (or max_batch).
+        Returns the new rows' slots (their ids while no compaction ran)."""
+        v = pad_rows(np.ascontiguousarray(vectors, dtype=np.float16))
+        assert v.shape[1] == self.dpad
+        old, m = self.n, v.shape[0]
+        self.vec = np.ascontiguousarray(np.concatenate([self.vec, v]))
+        self.edges = np.ascontiguousarray(np.concatenate(
+            [self.edges, np.full((m, self.R), 0xFFFFFFFF, np.uint32)]))
+        self.edist = np.ascontiguousarray(np.concatenate(
+            [self.edist, np.zeros((m, self.R), np.uint16)]))
+        self.counts = np.ascontiguousarray(np.concatenate([self.counts, np.zeros(m, np.uint8)]))
+        if self.deleted is not None:
+            words = (old + m + 31) // 32
+            d = np.zeros(words, np.uint32)
+            d[:self.deleted.shape[0]] = self.deleted
+            self.deleted = d
+        self.n = old + m
+        g = self._struct()
+        L = lib()
+        L.orc_append_range.argtypes = [C.POINTER(_Graph), C.c_uint32, C.c_uint32, C.c_float,
+                                       C.c_uint32]
+        L.orc_append_range(C.byref(g), old, m, float(alpha), int(max_batch))
+        return np.arange(old, old + m, dtype=np.int32)
+
     def search(self, queries: np.ndarray, k: int, beam_width: int, limit: int,
                max_result_size: int = 2048):
         q = pad_rows(queries)

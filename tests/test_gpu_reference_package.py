@@ -73,6 +73,21 @@ def test_reference_package_plain_path(refpkg, case, tmp_path):
         np.testing.assert_array_equal(v.cpu().numpy().view(np.uint16), X[5].view(np.uint16))
     finally:
         g.free()
+    # the reference package's append (python/jasper/__init__.py:673-697) on a
+    # graph of the first 80 % of the rows: ids continue the sequence and the
+    # appended rows find themselves
+    n0 = X.shape[0] * 4 // 5
+    ga = refpkg.Graph.build(Xd[:n0], n_neighbors=R, distance=metric, alpha=float(z["alpha"]))
+    try:
+        ids = ga.append(Xd[n0:], alpha=float(z["alpha"]))
+        assert ids.tolist() == list(range(n0, X.shape[0]))
+        if metric == "l2":
+            found, _ = ga.search(Xd[n0:], k=1, beam_width=64)
+            base, _ = ga.search(Xd[:300], k=1, beam_width=64)
+            own = (base[:, 0].cpu() == torch.arange(300)).float().mean().item()
+            assert (found[:, 0].cpu() == ids).float().mean().item() >= own - 0.03
+    finally:
+        ga.free()
     g2 = refpkg.Graph.load(str(p), dim=X.shape[1], n_neighbors=R, distance=metric)
     try:
         bw = int(z["bws"][-1])

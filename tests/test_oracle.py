@@ -184,3 +184,20 @@ def test_golden_directional_oracle_matches_reference(path):
             np.testing.assert_array_equal(oi, z[f"{key}_idx_bw{bw}"], err_msg=f"{kind} bw={bw}")
             np.testing.assert_array_equal(od.view(np.uint32), z[f"{key}_dist_bw{bw}"].view(np.uint32),
                                           err_msg=f"{kind} bw={bw}")
+
+
+def test_oracle_append_wires_new_rows():
+    """orc_append_range (append_batch, construct.cuh:1169-1265): appended
+    rows get edges and are found by a search for themselves; ids continue
+    the slot sequence."""
+    from jasper_b200 import synthetic
+    X = synthetic.gaussian(1600, 32, 95)
+    g = O.OracleGraph(X[:1200], 16)
+    g.build(1.2, 24)
+    ids = g.append(X[1200:], 1.2)
+    np.testing.assert_array_equal(ids, np.arange(1200, 1600))
+    assert g.n == 1600 and (g.counts[1200:] > 0).all()
+    # appended rows find themselves about as often as the built rows do
+    base, _, _, _ = g.search(X[:400], 1, 32, 64)
+    oi, _, _, _ = g.search(X[1200:], 1, 32, 64)
+    assert np.mean(oi[:, 0] == np.arange(1200, 1600)) >= np.mean(base[:, 0] == np.arange(400)) - 0.03
