@@ -295,8 +295,7 @@ def run_jasper(args):
 
     flush = torch.zeros(64 * 1024 * 1024, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream()
-    gbuf = (torch.empty(ws, 2, nloc_max, K, dtype=torch.int32, device=dev)
-            if ws > 1 and rank == 0 else None)
+    gbuf = torch.empty(ws, 2, nloc_max, K, dtype=torch.int32, device=dev) if ws > 1 else None
     pad_i = torch.full((nloc_max, K), -1, dtype=torch.int32, device=dev)
     pad_d = torch.full((nloc_max, K), 1e30, dtype=torch.float32, device=dev)
 

@@ -157,6 +157,10 @@ void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint3
   void* packed = nullptr;
   void* counter = nullptr;
   const bool aligned = (reinterpret_cast<uintptr_t>(queries) % 16) == 0;
+  // Prerotated graphs rotate the queries in the search kernel's prologue; a
+  // separate GEMM pass over packed queries is left only for very wide rows.
+  const bool fused_rotation = rotate && g.dpad <= jb::kFusedRotationMaxDpad;
+  if (fused_rotation) rotate = false;
   if (row_stride != g.dpad || !aligned || rotate) {
     pool_alloc(reinterpret_cast<void**>(&packed), size_t(nq) * g.dpad * 2, st, "alloc packed queries");
     cuda_check(cudaMemsetAsync(packed, 0, size_t(nq) * g.dpad * 2, st), "clear packed queries");
@@ -188,6 +192,7 @@ void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint3
   a.work_counter = static_cast<uint32_t*>(counter);
   a.stats = stats;
   a.seen_bits = seen;
+  a.rot_pad = fused_rotation ? g.dir.rotation_pad : nullptr;
   if (rq_margin >= 0.0f) {
     if (!g.dir.has_rabitq) throw std::runtime_error("graph has no RaBitQ codes built");
     if (!g.dir.rq_err)
@@ -598,13 +603,15 @@ int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* qu
     const uint16_t* q = queries;
     const size_t qbytes = size_t(n_queries) * g->dpad * 2;
     const bool aligned = (reinterpret_cast<uintptr_t>(queries) % 16) == 0;
-    if (row_stride != g->dpad || !aligned || d.prerotate) {
+    const bool fused_rotation = d.prerotate && g->dpad <= jb::kFusedRotationMaxDpad;
+    if (row_stride != g->dpad || !aligned || (d.prerotate && !fused_rotation)) {
       pool_alloc(reinterpret_cast<void**>(&packed), qbytes, st, "alloc queries");
       cuda_check(cudaMemsetAsync(packed, 0, qbytes, st), "clear queries");
       cuda_check(cudaMemcpy2DAsync(packed, size_t(g->dpad) * 2, queries, size_t(row_stride) * 2,
                                    size_t(g->dim) * 2, n_queries, cudaMemcpyDefault, st),
                  "pack queries");
-      if (d.prerotate) jb::rotate_rows_inplace(*g, static_cast<uint16_t*>(packed), n_queries, st);
+      if (d.prerotate && !fused_rotation)
+        jb::rotate_rows_inplace(*g, static_cast<uint16_t*>(packed), n_queries, st);
       q = static_cast<const uint16_t*>(packed);
     }
     pool_alloc(reinterpret_cast<void**>(&counter), 256, st, "alloc counter");
@@ -632,6 +639,7 @@ int jb_graph_directional_search(int64_t handle, int32_t kind, const uint16_t* qu
     a.out_idx = out_idx;
     a.out_dist = out_dist;
     a.work_counter = static_cast<uint32_t*>(counter);
+    a.rot_pad = fused_rotation ? d.rotation_pad : nullptr;
     try {
       jb::launch_dir_search(a, st);
     } catch (...) {

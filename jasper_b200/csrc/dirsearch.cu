@@ -136,12 +136,16 @@ __global__ void __launch_bounds__(128) dir_search_kernel(DirSearchArgs a) {
     q = __shfl_sync(kFull, q, 0);
     if (q >= a.nq) break;
 
-    {  // query row into shared memory
+    {  // query row into shared memory (raw into qu first when it is rotated here)
       const uint4* src = reinterpret_cast<const uint4*>(a.queries + size_t(q) * dpad);
-      uint4* dst = reinterpret_cast<uint4*>(qh);
+      uint4* dst = reinterpret_cast<uint4*>(a.rot_pad != nullptr ? qu : qh);
       for (uint32_t c = lane; c < nv4; c += 32) dst[c] = ldg16(src + c);
     }
     __syncwarp();
+    if (a.rot_pad != nullptr) {
+      rotate_query_warp(qu, qh, a.rot_pad, g.dim, dpad, lane);
+      __syncwarp();
+    }
 
     float q_sq = 0.0f;
     if constexpr (KIND == kDirPq) {

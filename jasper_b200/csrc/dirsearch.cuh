@@ -29,6 +29,9 @@ struct DirSearchArgs {
   int32_t* out_idx;
   float* out_dist;
   uint32_t* work_counter;   // zeroed
+  // Optional prerotation of the queries in the kernel prologue (dpad x dpad
+  // fp16, row i = column i of P), as in SearchArgs::rot_pad.
+  const uint16_t* rot_pad;
 };
 
 void launch_dir_search(const DirSearchArgs& a, cudaStream_t stream);

@@ -56,6 +56,40 @@ __device__ __forceinline__ uint4 ldg16(const uint4* p) {
   return r;
 }
 
+// The query's prerotation, fused into a search prologue (one warp per query):
+// y_i = fp16(sum_k x_k P[k][i]) for i < d, 0 for d <= i < dpad, with the sum
+// taken in k order by fp32 fma -- the order of the SIMT rotation GEMM
+// (rotate.cu, rotate_kernel), which walks k in tiles of 32 and adds the zero
+// products of a partial last tile (one fma(0, 0, acc) is the same as several).
+// x, y: padded fp16 rows in shared memory (x's pad lanes zero); Mp: dpad x
+// dpad, row i = column i of P, zero padded (16-byte aligned rows).
+static __device__ __noinline__ void rotate_query_warp(const uint16_t* x, uint16_t* y,
+                                                  const uint16_t* Mp, uint32_t d, uint32_t dpad,
+                                                  int lane) {
+  const uint4* x4 = reinterpret_cast<const uint4*>(x);
+  for (uint32_t i = lane; i < dpad; i += 32) {
+    float acc = 0.0f;
+    if (i < d) {
+      const uint4* row = reinterpret_cast<const uint4*>(Mp + size_t(i) * dpad);
+      for (uint32_t c = 0; c < dpad / 8; c++) {
+        const uint4 pw = ldg16(row + c), xw = x4[c];
+        const uint32_t pv[4] = {pw.x, pw.y, pw.z, pw.w}, xv[4] = {xw.x, xw.y, xw.z, xw.w};
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+          const float2 pf = __half22float2(*reinterpret_cast<const __half2*>(&pv[w]));
+          const float2 xf = __half22float2(*reinterpret_cast<const __half2*>(&xv[w]));
+          const uint32_t k = 8 * c + 2 * w;
+          if (k < d) acc = __fmaf_rn(xf.x, pf.x, acc);
+          if (k + 1 < d) acc = __fmaf_rn(xf.y, pf.y, acc);
+        }
+      }
+      if (d % 32 != 0) acc = __fmaf_rn(0.0f, 0.0f, acc);
+    }
+    const __half h = __float2half_rn(acc);
+    y[i] = i < d ? *reinterpret_cast<const uint16_t*>(&h) : uint16_t(0);
+  }
+}
+
 // One 16-byte chunk (8 halves) of the L2 sum, element order 0..7, each term
 // fused as fma(d, d, acc): the reference's per-lane accumulation
 // (include/jasper/distance/distance.cuh:131-141).

@@ -520,18 +520,32 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC, BWCAP>())
     const uint16_t* qrow = a.use_range
         ? g.vec + size_t(a.query_start + q - g.global_offset) * dpad
         : a.queries + size_t(q) * dpad;
+    bool q_in_smem = false;
+    if (a.rot_pad != nullptr) {
+      // Prerotated graph: rotate the query here (rotate_query_warp).  The
+      // visited table's slots are free until it is cleared below, so the raw
+      // row (and, for the register layouts, the rotated one) sit there.
+      uint16_t* raw = reinterpret_cast<uint16_t*>(sm.hash);
+      uint16_t* rot = kRegQ ? raw + dpad : sm.query;
+      const uint4* src = reinterpret_cast<const uint4*>(qrow);
+      for (int c = lane; c < nchunks; c += 32) reinterpret_cast<uint4*>(raw)[c] = ldg16(src + c);
+      __syncwarp();
+      rotate_query_warp(raw, rot, a.rot_pad, g.dim, dpad, lane);
+      __syncwarp();
+      qrow = rot;
+      q_in_smem = true;
+    }
     if constexpr (kTile) {
       build_qtile<MAXC>(reinterpret_cast<float*>(sm.qpairs), qrow, nchunks, lane);
       __syncwarp();
     } else if constexpr (kRegQ) {
       build_qpairs<MAXC, METRIC>(sm.qpairs, qrow, nchunks, lane);
       __syncwarp();
-    } else {
+    } else if (!q_in_smem) {
       const uint4* src = reinterpret_cast<const uint4*>(qrow);
       uint4* dst = reinterpret_cast<uint4*>(sm.query);
       for (int c = lane; c < nchunks; c += 32) dst[c] = ldg16(src + c);
     }
-    for (uint32_t i = lane; i < hsize; i += 32) sm.hash[i] = kHashEmpty;
     // RaBitQ filter: the query's 4-bit planes, offsets and centroid terms.
     float rq_vl = 0.0f, rq_delta = 0.0f, rq_gadd = 0.0f, rq_lq = 0.0f;
     int rq_S = 0;
@@ -584,6 +598,8 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC, BWCAP>())
       rq_gadd = METRIC == kIP ? -acc_ip : acc_l2;
       rq_lq = __fmul_rn(a.rq_margin, __fsqrt_rn(acc_l2));
     }
+    __syncwarp();  // every read of a rotated query in the table's slots is done
+    for (uint32_t i = lane; i < hsize; i += 32) sm.hash[i] = kHashEmpty;
     __syncwarp();
 
     uint32_t first_evals = 0;  // per lane; summed at the end (stats only)

@@ -36,7 +36,14 @@ struct SearchArgs {
   const float* rq_centroid;  // [dim]
   const float* rq_err;       // [n]
   float rq_margin;
+  // Optional prerotation of the queries (not of the use_range rows): dpad x
+  // dpad fp16, row i = column i of P; the kernel rotates each query in its
+  // prologue.  Needs dpad <= kFusedRotationMaxDpad.
+  const uint16_t* rot_pad;
 };
+
+// Largest padded dimension whose query rotation fits the prologue's scratch.
+constexpr uint32_t kFusedRotationMaxDpad = 1024;
 
 // Bytes of device scratch a search launch needs (the work counter).
 constexpr size_t kSearchScratchBytes = 256;

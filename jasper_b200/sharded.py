@@ -41,36 +41,30 @@ def split_queries(n_queries: int, world: int, rank: int) -> slice:
     return slice(off, off + cnt)
 
 
-def _pack(local_idx: torch.Tensor, local_dist: torch.Tensor) -> torch.Tensor:
-    """[2, nq, k] int32: ids, then the distances' bit patterns."""
-    nq, k = local_idx.shape
-    packed = torch.empty(2, nq, k, dtype=torch.int32, device=local_idx.device)
-    packed[0].copy_(local_idx)
-    packed[1].copy_(local_dist.to(torch.float32).view(torch.int32))
-    return packed
-
-
 def gather_topk(local_idx: torch.Tensor, local_dist: torch.Tensor, root: int = 0,
                 group=None, out: torch.Tensor | None = None
                 ) -> tuple[torch.Tensor, torch.Tensor] | None:
-    """Gather every rank's [nq, k] top-k to ``root`` with ONE collective:
-    each rank sends its ids and distance bits as one [2, nq, k] buffer into
-    ``root``'s [world, 2, nq, k] buffer (``out`` if given).  Returns
-    ``(ids, dists)`` as [world, nq, k] views of that buffer on ``root``
-    (shard stride 2 * nq * k, which ``merge_topk`` reads in place) and None
-    elsewhere."""
+    """Collect every rank's [nq, k] top-k on ``root`` with ONE collective.
+    Each rank packs its ids and distance bits into one [2, nq, k] int32
+    slice of a [world, 2, nq, k] buffer (``out`` if given: reused across
+    calls) and the slices are exchanged with all_gather_into_tensor (one
+    NCCL all-gather: each shard's 8 nq k bytes reach every rank; the
+    lowest host cost of the collectives that gather).  Returns ``(ids,
+    dists)`` as [world, nq, k] views of the buffer on ``root`` (shard stride
+    2 nq k, which ``merge_topk`` reads in place) and None elsewhere."""
     import torch.distributed as dist
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
-    packed = _pack(local_idx, local_dist)
-    if rank == root:
-        nq, k = local_idx.shape
-        if out is None or out.shape != (world, 2, nq, k):
-            out = torch.empty(world, 2, nq, k, dtype=torch.int32, device=packed.device)
-        dist.gather(packed, list(out.unbind(0)), dst=root, group=group)
-        return out[:, 0], out[:, 1].view(torch.float32)
-    dist.gather(packed, None, dst=root, group=group)
-    return None
+    nq, k = local_idx.shape
+    if out is None or out.shape != (world, 2, nq, k) or out.device != local_idx.device:
+        out = torch.empty(world, 2, nq, k, dtype=torch.int32, device=local_idx.device)
+    mine = out[rank]
+    mine[0].copy_(local_idx)
+    mine[1].copy_(local_dist.to(torch.float32).view(torch.int32))
+    dist.all_gather_into_tensor(out.view(-1), mine.reshape(-1), group=group)
+    if rank != root:
+        return None
+    return out[:, 0], out[:, 1].view(torch.float32)
 
 
 def merge_topk(shard_idx: torch.Tensor, shard_dist: torch.Tensor,
@@ -137,14 +131,14 @@ class ShardedGraph:
         li, ld = self.search_local(queries, k, beam_width)
         if ev is not None:
             ev[1].record()
+        if self._gather_buf is None or self._gather_buf.shape[2:] != li.shape:
+            import torch.distributed as dist
+            self._gather_buf = torch.empty(dist.get_world_size(self.group), 2, *li.shape,
+                                           dtype=torch.int32, device=li.device)
         g = gather_topk(li, ld, root=root, group=self.group, out=self._gather_buf)
         if ev is not None:
             ev[2].record()
-        if g is None:
-            out = None
-        else:
-            self._gather_buf = g[0]._base if g[0]._base is not None else None
-            out = merge_topk(g[0], g[1], k)
+        out = None if g is None else merge_topk(g[0], g[1], k)
         if ev is not None:
             ev[3].record()
             phases.append(ev)

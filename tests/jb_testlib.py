@@ -166,12 +166,15 @@ def dir_search_kind(h: int, kind: int, Q: np.ndarray, k: int, bw: int, limit: in
     return oi.cpu().numpy(), od.cpu().numpy()
 
 
-def rotate_on_device(Q: np.ndarray, dim: int, seed: int) -> np.ndarray:
-    """Rows rotated by the same tensor-core GEMM the search uses, as fp16 [n, dim]."""
+def rotate_on_device(Q: np.ndarray, dim: int, seed: int, tensor_cores: bool = False) -> np.ndarray:
+    """Rows rotated on the device, as fp16 [n, dim].  By default in the SIMT
+    GEMM's summation order, which is the order the search kernels use when
+    they rotate each query in their prologue; tensor_cores=True gives the
+    tcgen05 GEMM that rotates a graph's rows."""
     import torch
     x = torch.from_numpy(O.pad_rows(Q)).cuda()
     y = torch.empty_like(x)
-    _lib.call("jb_rotate_rows", dim, seed, x.data_ptr(), y.data_ptr(), x.shape[0], 1,
-              torch.cuda.current_stream().cuda_stream)
+    _lib.call("jb_rotate_rows", dim, seed, x.data_ptr(), y.data_ptr(), x.shape[0],
+              1 if tensor_cores else 0, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
     return y.cpu().numpy().view(np.float16)[:, :dim]

@@ -162,13 +162,18 @@ def test_prerotated_construct_and_search(cuda, metric):
         cent_np = D.pq_train(Yh, g.edges, g.counts, kr, n_train=5000, iters=8)
         art_np = dict(art, lsh_c=c_np, lsh_norm_denom=nd_np, pq_centroids=cent_np,
                       pq_codes=O.pq_codes_exact(g, cent_np))
-        # queries are rotated inside the call: equal to searching rotated queries
-        Qr = (Q.astype(np.float32) @ A.T).astype(np.float16)
+        # queries are rotated inside the search kernel's prologue, in the
+        # SIMT rotation GEMM's order: the results equal the restatement's
+        # search of the queries rotated by that GEMM, bit for bit
+        Qr = T.rotate_on_device(Q, dim, 42)
+        Qf = (Q.astype(np.float32) @ A.T).astype(np.float16)
+        assert np.mean(np.abs(Qr.astype(np.float32) - Qf.astype(np.float32)) <=
+                       2 * 2.0 ** -10 * np.maximum(np.abs(Qf.astype(np.float32)), 2.0 ** -14)
+                       + 1e-3) > 0.999
         for which in ("lsh", "pq"):
             ji, jd = T.dir_search(h, which, Q, 10, 64)
             oi, od = O.dir_search(g, which, art, Qr, 10, 64, 128)
-            agree = (ji == oi).mean()
-            assert agree > 0.97, (which, agree)   # Qr rounding differs from the device GEMM's
+            T.assert_same_results(ji, jd, oi, od, msg=which)
             # estimator quality: recall@10 with the device-built payloads is
             # no worse (within 0.05) than with payloads built by the numpy
             # restatement of the same builders on the same graph
