@@ -63,6 +63,7 @@ SIGNATURES: dict[str, list] = {
     "jb_graph_get_directional_flags": [_I64, C.POINTER(_I32)],
     "jb_graph_directional_search": [_I64, _I32, _P, _U64, _U32, _P, _P, _U32, _U32, _U32, _P],
     "jb_merge_topk": [_P, _P, _U32, _U64, _U32, _P, _P, _P],
+    "jb_search_set_warps_per_query": [_I32],
     "jb_graph_append": [_I64, _P, _U64, _U32, C.c_double, _P, _P],
     "jb_merge_topk_strided": [_P, _P, _U64, _U32, _U64, _U32, _P, _P, _P],
     "jb_graph_construct_directional": [_P, _U64, _U32, _U32, _U32, _I32, C.c_double, _U64, _I32,

@@ -232,6 +232,10 @@ const char* jb_last_error(void) { return g_last_error.c_str(); }
 
 int jb_abi_version(void) { return 1; }
 
+int jb_search_set_warps_per_query(int32_t warps_per_query) {
+  return guarded([&] { jb::set_search_mode(warps_per_query); });
+}
+
 int jb_graph_create(const uint16_t* vectors, uint64_t n, uint32_t dim, uint32_t row_stride,
                     uint32_t n_neighbors, int32_t metric, int32_t on_host, int64_t* out_handle) {
   return guarded([&] {

@@ -34,8 +34,10 @@
 // Loop bounds follow beam_search.cuh:129-203: at most limit + 1 rounds; a
 // round expands the first unvisited beam entry; when the expansion count
 // reaches max_result_size the loop stops before adding that node's neighbours.
+#include <atomic>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <stdexcept>
 #include <string>
 #include <utility>
@@ -926,6 +928,429 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC, BWCAP>())
   JB_CLK_FLUSH
 }
 
+// ── CTA per query (few queries per GPU) ─────────────────────────────────────
+// The warp-per-query kernel needs thousands of queries to fill a B200; with
+// a few hundred per GPU (a split query batch on many GPUs, or 1k wide rows)
+// each query's latency decides the time.  Here one CTA of W warps owns a
+// query and the warps share each expansion's candidate distances:
+//   every warp     -- choose_new_frontier from the shared beam (identical
+//                     result in every warp, so no barrier is needed for it);
+//   warp 0         -- visited-table upkeep, neighbour list, filters;   B1
+//   all W warps    -- the candidates' distances, 16-row (tile and shared-
+//                     memory layouts) slices dealt round-robin;       B2
+//   warp 0         -- keep / sort the candidates and merge the beam;  B3
+// Every decision that steers the loop is read from shared memory after a
+// barrier, so all warps take the same path and reach every barrier.  The
+// traversal, the distances (same summation order) and the output are those
+// of the warp-per-query kernel.
+template <int MAXC>
+__device__ __forceinline__ void cta_tile_rows(const WarpSmem& sm, const GraphView& g, const float* qs,
+                                              int base, int m, int tile, int s, uint32_t dpad,
+                                              int nchunks, uint32_t* seen, uint32_t& first) {
+  constexpr int SL = JB_T4_SLOTS;
+  const int nslot = min(SL, (m - base + 7) >> 3);
+  uint4 u[SL][MAXC];
+  uint32_t rid[SL];
+#pragma unroll
+  for (int i = 0; i < SL; i++) {
+    const int j = base + tile + 8 * i;
+    const bool act = i < nslot && j < m;
+    rid[i] = act ? sm.cand_ids[j] : kInvalid;
+    const uint4* row = reinterpret_cast<const uint4*>(
+        g.vec + size_t(act ? rid[i] - g.global_offset : 0) * dpad);
+#pragma unroll
+    for (int k = 0; k < MAXC; k++) {
+      const int c = s + 4 * k;
+      u[i][k] = (act && c < nchunks) ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+    }
+  }
+#pragma unroll
+  for (int p = 0; p < SL / 2; p++) {
+    if (2 * p >= nslot) break;
+    const float2 v = tile4_pair_sum<MAXC>(tile4_pair_chain<MAXC>(qs, u[2 * p], u[2 * p + 1]));
+    if (s == 0) {
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int i = 2 * p + h;
+        const int j = base + tile + 8 * i;
+        if (rid[i] != kInvalid) {
+          sm.cand_keys[j] = make_key(h ? v.y : v.x, rid[i]);
+          if (seen != nullptr) {
+            const uint32_t l = rid[i] - g.global_offset;
+            if (!(atomicOr(&seen[l >> 5], 1u << (l & 31)) & (1u << (l & 31)))) first++;
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int METRIC>
+__device__ __forceinline__ void cta_smemq_rows(const WarpSmem& sm, const GraphView& g, int base,
+                                               int m, int tile, int s, uint32_t dpad, int nchunks,
+                                               uint32_t* seen, uint32_t& first) {
+  const int i0 = base + tile, i1 = base + tile + 8;
+  const bool a0 = i0 < m, a1 = i1 < m;
+  const uint32_t id0 = a0 ? sm.cand_ids[i0] : g.global_offset;
+  const uint32_t id1 = a1 ? sm.cand_ids[i1] : id0;
+  const uint4* r0 = reinterpret_cast<const uint4*>(g.vec + size_t(id0 - g.global_offset) * dpad);
+  const uint4* r1 = reinterpret_cast<const uint4*>(g.vec + size_t(id1 - g.global_offset) * dpad);
+  const float2 dd = dist_smemq2<METRIC>(sm.query, r0, a0, r1, a1, nchunks, s);
+  if (s == 0) {
+    if (a0) sm.cand_keys[i0] = make_key(dd.x, id0);
+    if (a1) sm.cand_keys[i1] = make_key(dd.y, id1);
+    if (seen != nullptr) {
+      const uint32_t l0 = id0 - g.global_offset, l1 = id1 - g.global_offset;
+      if (a0 && !(atomicOr(&seen[l0 >> 5], 1u << (l0 & 31)) & (1u << (l0 & 31)))) first++;
+      if (a1 && !(atomicOr(&seen[l1 >> 5], 1u << (l1 & 31)) & (1u << (l1 & 31)))) first++;
+    }
+  }
+}
+
+// MAXC: 1..4 = tile-of-4 layout (L2, dpad <= 128); 0 = shared-memory query
+// (any dpad, L2 or inner product).
+template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC, int W>
+__global__ void __launch_bounds__(32 * W, 4) beam_search_cta_kernel(SearchArgs a) {
+  constexpr bool kTile = MAXC > 0;
+  extern __shared__ __align__(16) char smem_raw[];
+  __shared__ uint32_t s_q, s_m, s_cnt, s_flip, s_first;
+  const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
+  const uint32_t dpad = a.g.dpad;
+  const uint32_t rq_nw = a.rq_on ? (a.g.dim + 31) / 32 : 0;
+  const size_t per_q = warp_smem_bytes(BWCAP, HBITS, dpad, MAXC, 4 * rq_nw);
+  WarpSmem sm = carve(smem_raw, BWCAP, HBITS);
+  uint32_t* rq_planes = reinterpret_cast<uint32_t*>(smem_raw + per_q - align16(size_t(4) * rq_nw * 4));
+  const int tile = lane >> 2, s = lane & 3;
+  const int nchunks = int(dpad / 8);
+  const GraphView& g = a.g;
+  const uint32_t hsize = 1u << HBITS;
+  const uint32_t R = g.R;
+  const uint32_t bw = a.bw;
+  const float* qs = reinterpret_cast<const float*>(sm.qpairs) + s * (8 * MAXC + 4);
+
+  for (;;) {
+    if (threadIdx.x == 0) s_q = atomicAdd(a.work_counter, 1u);
+    __syncthreads();
+    const uint32_t q = s_q;
+    if (q >= a.nq) break;
+    uint32_t* seen = a.seen_bits != nullptr ? a.seen_bits + size_t(q) * ((g.n + 31) / 32) : nullptr;
+
+    // ── prologue: query layout and RaBitQ terms (warp 0), table clear (all)
+    float rq_vl = 0.0f, rq_delta = 0.0f, rq_gadd = 0.0f, rq_lq = 0.0f;
+    int rq_S = 0;
+    if (wid == 0) {
+      const uint16_t* qrow = a.queries + size_t(q) * dpad;
+      if (a.rot_pad != nullptr) {
+        uint16_t* raw = reinterpret_cast<uint16_t*>(sm.hash);
+        uint16_t* rot = kTile ? raw + dpad : sm.query;
+        const uint4* src = reinterpret_cast<const uint4*>(qrow);
+        for (int c = lane; c < nchunks; c += 32) reinterpret_cast<uint4*>(raw)[c] = ldg16(src + c);
+        __syncwarp();
+        rotate_query_warp(raw, rot, a.rot_pad, g.dim, dpad, lane);
+        __syncwarp();
+        qrow = rot;
+      } else if constexpr (!kTile) {
+        const uint4* src = reinterpret_cast<const uint4*>(qrow);
+        for (int c = lane; c < nchunks; c += 32) reinterpret_cast<uint4*>(sm.query)[c] = ldg16(src + c);
+        __syncwarp();
+        qrow = sm.query;
+      }
+      if constexpr (kTile) build_qtile<(kTile ? MAXC : 1)>(reinterpret_cast<float*>(sm.qpairs), qrow, nchunks, lane);
+      if (a.rq_on) {
+        const __half* qv = reinterpret_cast<const __half*>(qrow);
+        const uint32_t dim = g.dim;
+        float vl = __int_as_float(0x7F800000), vr = -vl;
+        for (uint32_t i = lane; i < dim; i += 32) {
+          const float x = __half2float(qv[i]);
+          vl = fminf(vl, x);
+          vr = fmaxf(vr, x);
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) {
+          vl = fminf(vl, __shfl_xor_sync(kFull, vl, d));
+          vr = fmaxf(vr, __shfl_xor_sync(kFull, vr, d));
+        }
+        const float range = __fsub_rn(vr, vl);
+        const float inv = range > 0.0f ? __fdiv_rn(15.0f, range) : 0.0f;
+        int S = 0;
+        for (uint32_t w = 0; w < rq_nw; w++) {
+          const uint32_t i = 32 * w + lane;
+          int qq = 0;
+          if (i < dim) {
+            qq = __float2int_rn(__fmul_rn(__fsub_rn(__half2float(qv[i]), vl), inv));
+            qq = qq < 0 ? 0 : (qq > 15 ? 15 : qq);
+          }
+          S += qq;
+#pragma unroll
+          for (int p = 0; p < 4; p++) {
+            const uint32_t bits = __ballot_sync(kFull, (qq >> p) & 1);
+            if (lane == 0) rq_planes[p * rq_nw + w] = bits;
+          }
+        }
+#pragma unroll
+        for (int d = 16; d > 0; d >>= 1) S += __shfl_xor_sync(kFull, S, d);
+        float acc_ip = 0.0f, acc_l2 = 0.0f;
+        for (uint32_t i = lane; i < dim; i += 32) {
+          const float x = __half2float(qv[i]);
+          const float ci = __ldg(a.rq_centroid + i);
+          acc_ip = __fmaf_rn(ci, x, acc_ip);
+          const float dd = __fsub_rn(x, ci);
+          acc_l2 = __fmaf_rn(dd, dd, acc_l2);
+        }
+        acc_ip = warp_sum_xor(acc_ip);
+        acc_l2 = warp_sum_xor(acc_l2);
+        rq_vl = vl;
+        rq_delta = __fdiv_rn(range, 15.0f);
+        rq_S = S;
+        rq_gadd = METRIC == kIP ? -acc_ip : acc_l2;
+        rq_lq = __fmul_rn(a.rq_margin, __fsqrt_rn(acc_l2));
+      }
+    }
+    if (threadIdx.x == 0) s_first = 0;
+    __syncthreads();  // every read of a query staged in the table's slots is done
+    for (uint32_t i = threadIdx.x; i < hsize; i += 32 * W) sm.hash[i] = kHashEmpty;
+    __syncthreads();
+
+    // ── seed with the medoid (warp 0)
+    uint64_t* cur = sm.beam0;
+    uint64_t* nxt = sm.beam1;
+    uint32_t first = 0, n_hash = 1, expansions = 0, deg_sum = 0, evals = 1, resets = 0;
+    if (wid == 0) {
+      if (lane == 0) {
+        sm.cand_ids[0] = g.medoid;
+        hash_insert(sm.hash, HBITS, g.medoid);
+      }
+      __syncwarp();
+      if constexpr (kTile) cta_tile_rows<(kTile ? MAXC : 1)>(sm, g, qs, 0, 1, tile, s, dpad, nchunks, seen, first);
+      else cta_smemq_rows<METRIC>(sm, g, 0, 1, tile, s, dpad, nchunks, seen, first);
+      __syncwarp();
+      if (lane == 0) cur[0] = sm.cand_keys[0];
+    }
+    uint32_t cnt = 1;
+    __syncthreads();
+
+    uint32_t loop_count = 0;
+    while (loop_count <= a.limit) {
+      loop_count++;
+      int pos = -1;  // choose_new_frontier, identical in every warp
+      for (uint32_t b0 = 0; b0 < cnt; b0 += 32) {
+        const uint32_t i = b0 + lane;
+        const bool unv = i < cnt && !key_visited(cur[i]);
+        const uint32_t bal = __ballot_sync(kFull, unv);
+        if (bal) { pos = int(b0) + __ffs(bal) - 1; break; }
+      }
+      if (pos < 0) break;
+      const uint64_t fkey = cur[pos];
+      expansions++;
+      if (expansions == a.max_result_size) break;
+      const uint32_t u = key_id(fkey);
+
+      if (wid == 0) {
+        if (n_hash + R > kHashFillNum * (hsize / kHashFillDen)) {
+          for (uint32_t i = lane; i < hsize; i += 32) sm.hash[i] = kHashEmpty;
+          __syncwarp();
+          for (uint32_t i = lane; i < cnt; i += 32) hash_insert(sm.hash, HBITS, key_id(cur[i]));
+          n_hash = cnt;
+          resets++;
+          __syncwarp();
+        }
+        const uint32_t lu = u - g.global_offset;
+        const uint32_t ne = g.counts[lu];
+        const uint32_t* el = g.edges + size_t(lu) * R;
+        const uint32_t nb0 = lane < R ? __ldg(el + lane) : kInvalid;
+        const uint32_t nb1 = lane + 32 < R ? __ldg(el + lane + 32) : kInvalid;
+        deg_sum += ne;
+        const bool f0 = (lane < ne) && (nb0 - g.global_offset < g.n) && hash_insert(sm.hash, HBITS, nb0);
+        const uint32_t b0 = __ballot_sync(kFull, f0);
+        const bool f1 = (lane + 32 < ne) && (nb1 - g.global_offset < g.n) && hash_insert(sm.hash, HBITS, nb1);
+        const uint32_t b1 = __ballot_sync(kFull, f1);
+        const uint32_t lt = (1u << lane) - 1u;
+        if (f0) sm.cand_ids[__popc(b0 & lt)] = nb0;
+        if (f1) sm.cand_ids[__popc(b0) + __popc(b1 & lt)] = nb1;
+        int m = __popc(b0) + __popc(b1);
+        n_hash += m;
+        __syncwarp();
+        if (a.rq_on && cnt == bw && m > 0) {
+          const float tau = key_dist(cur[bw - 1]);
+          bool k0 = false, k1 = false;
+          uint32_t c0 = 0, c1 = 0;
+          if (lane < m) {
+            c0 = sm.cand_ids[lane];
+            const uint32_t l = c0 - g.global_offset;
+            const float est = rabitq_est(a, l, rq_planes, rq_nw, g.dim, rq_vl, rq_delta, rq_S,
+                                         rq_gadd, METRIC == kIP);
+            k0 = !(__fsub_rn(est, __fmul_rn(rq_lq, __ldg(a.rq_err + l))) > tau);
+          }
+          if (lane + 32 < m) {
+            c1 = sm.cand_ids[lane + 32];
+            const uint32_t l = c1 - g.global_offset;
+            const float est = rabitq_est(a, l, rq_planes, rq_nw, g.dim, rq_vl, rq_delta, rq_S,
+                                         rq_gadd, METRIC == kIP);
+            k1 = !(__fsub_rn(est, __fmul_rn(rq_lq, __ldg(a.rq_err + l))) > tau);
+          }
+          const uint32_t kb0 = __ballot_sync(kFull, k0), kb1 = __ballot_sync(kFull, k1);
+          __syncwarp();
+          if (k0) sm.cand_ids[__popc(kb0 & lt)] = c0;
+          if (k1) sm.cand_ids[__popc(kb0) + __popc(kb1 & lt)] = c1;
+          m = __popc(kb0) + __popc(kb1);
+        }
+        evals += m;
+        if (lane == 0) s_m = uint32_t(m);
+      }
+      __syncthreads();  // B1: candidates listed
+      const int m = int(s_m);
+      if (threadIdx.x == 0) cur[pos] = fkey | 1ull;
+      // distances: 16-row slices dealt round-robin over the warps
+      for (int base = 16 * wid; base < m; base += 16 * W) {
+        if constexpr (kTile) cta_tile_rows<(kTile ? MAXC : 1)>(sm, g, qs, base, m, tile, s, dpad, nchunks, seen, first);
+        else cta_smemq_rows<METRIC>(sm, g, base, m, tile, s, dpad, nchunks, seen, first);
+      }
+      __syncthreads();  // B2: candidate keys written
+
+      if (wid == 0) {
+        uint64_t v0 = lane < m ? sm.cand_keys[lane] : kKeyMax;
+        uint64_t v1 = lane + 32 < m ? sm.cand_keys[lane + 32] : kKeyMax;
+        if (cnt == bw) {
+          const uint64_t worst = cur[bw - 1] | 1ull;
+          if (v0 > worst) v0 = kKeyMax;
+          if (v1 > worst) v1 = kKeyMax;
+        }
+        const uint32_t k0 = __ballot_sync(kFull, v0 != kKeyMax);
+        const uint32_t k1 = __ballot_sync(kFull, v1 != kKeyMax);
+        const int kept = __popc(k0) + __popc(k1);
+        __syncwarp();
+        bool sorted = true;
+        if (kept > 0 && kept <= 32) {
+          const uint32_t lt = (1u << lane) - 1u;
+          if (v0 != kKeyMax) sm.cand_keys[__popc(k0 & lt)] = v0;
+          if (v1 != kKeyMax) sm.cand_keys[__popc(k0) + __popc(k1 & lt)] = v1;
+          __syncwarp();
+          if (kept <= kCountMerge) {
+            sorted = false;
+          } else {
+            uint64_t v = lane < kept ? sm.cand_keys[lane] : kKeyMax;
+            v = warp_sort32(v, lane);
+            sm.cand_keys[lane] = v;
+          }
+        } else if (kept > 32) {
+          warp_sort64(v0, v1, lane);
+          sm.cand_keys[lane] = v0;
+          sm.cand_keys[lane + 32] = v1;
+        }
+        __syncwarp();
+        if (kept > 0) {
+          if (!sorted) {
+            for (uint32_t i = lane; i < cnt; i += 32) {
+              const uint64_t b = cur[i];
+              uint32_t r = 0;
+              for (int j = 0; j < kept; j++) r += sm.cand_keys[j] < b;
+              if (i + r < bw) nxt[i + r] = b;
+            }
+            if (lane < kept) {
+              const uint64_t c = sm.cand_keys[lane];
+              uint32_t r = 0;
+              for (int j = 0; j < kept; j++) r += sm.cand_keys[j] < c;
+              const uint32_t p = r + lower_rank(cur, int(cnt), c);
+              if (p < bw) nxt[p] = c;
+            }
+          } else {
+            for (uint32_t i = lane; i < cnt; i += 32) {
+              const uint64_t b = cur[i];
+              const uint32_t p = i + lower_rank(sm.cand_keys, kept, b);
+              if (p < bw) nxt[p] = b;
+            }
+            for (int j = lane; j < kept; j += 32) {
+              const uint64_t c = sm.cand_keys[j];
+              const uint32_t p = j + lower_rank(cur, int(cnt), c);
+              if (p < bw) nxt[p] = c;
+            }
+          }
+        }
+        if (lane == 0) {
+          s_flip = kept > 0 ? 1u : 0u;
+          s_cnt = kept > 0 ? min(bw, cnt + uint32_t(kept)) : cnt;
+        }
+      }
+      __syncthreads();  // B3: beam merged
+      cnt = s_cnt;
+      if (s_flip) { uint64_t* t = cur; cur = nxt; nxt = t; }
+    }
+
+    if (a.stats != nullptr && s == 0) atomicAdd(&s_first, first);
+    __syncthreads();
+    // output: the first k non-deleted entries (beam_search.cuh:205-222)
+    if (wid == 0) {
+      uint32_t out = 0;
+      for (uint32_t b0 = 0; b0 < cnt && out < a.k; b0 += 32) {
+        const uint32_t i = b0 + lane;
+        uint32_t id = 0;
+        bool ok = false;
+        if (i < cnt) {
+          id = key_id(cur[i]);
+          const uint32_t l = id - g.global_offset;
+          ok = !(g.deleted != nullptr && ((g.deleted[l >> 5] >> (l & 31)) & 1u));
+        }
+        const uint32_t bal = __ballot_sync(kFull, ok);
+        const uint32_t p = out + __popc(bal & ((1u << lane) - 1u));
+        if (ok && p < a.k) {
+          const uint32_t sid = g.ids_identity ? id : g.slot_to_id[id - g.global_offset];
+          a.out_idx[size_t(q) * a.k + p] = int32_t(sid);
+          a.out_dist[size_t(q) * a.k + p] = key_dist(cur[i]);
+        }
+        out += __popc(bal);
+      }
+      for (uint32_t p = out + lane; p < a.k; p += 32) {
+        a.out_idx[size_t(q) * a.k + p] = -1;
+        a.out_dist[size_t(q) * a.k + p] = 1e30f;
+      }
+      if (lane == 0 && a.stats != nullptr) {
+        a.stats[size_t(q) * 5 + 0] = expansions;
+        a.stats[size_t(q) * 5 + 1] = deg_sum;
+        a.stats[size_t(q) * 5 + 2] = evals;
+        a.stats[size_t(q) * 5 + 3] = resets;
+        a.stats[size_t(q) * 5 + 4] = seen != nullptr ? s_first : evals;
+      }
+    }
+    __syncthreads();  // shared state is reused by the next query
+  }
+}
+
+// The shared-memory opt-in and the occupancy query cost a few microseconds
+// each, so they are cached per (kernel, device, shared memory).  The opt-in
+// is a maximum: it is only ever raised, never lowered by a smaller launch, so
+// a cached larger launch stays valid.
+struct LaunchShape { int sms, per_sm; };
+using SearchKernel = void (*)(SearchArgs);
+
+LaunchShape launch_shape(SearchKernel kern, int threads, size_t smem) {
+  static std::mutex m;
+  static std::map<std::tuple<const void*, int, size_t>, LaunchShape> cache;
+  static std::map<std::pair<const void*, int>, size_t> opted;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const void* key = reinterpret_cast<const void*>(kern);
+  std::lock_guard<std::mutex> lock(m);
+  size_t& cur = opted[{key, dev}];
+  if (smem > cur) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    cur = smem;
+  }
+  auto it = cache.find({key, dev, smem});
+  if (it != cache.end()) return it->second;
+  LaunchShape L{};
+  cudaDeviceGetAttribute(&L.sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&L.per_sm, kern, threads, smem);
+  if (L.per_sm < 1) L.per_sm = 1;
+  cache[{key, dev, smem}] = L;
+  return L;
+}
+
+void check_launch() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("search launch: ") + cudaGetErrorString(e));
+}
+
 template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC>
 void launch_t(const SearchArgs& a, cudaStream_t stream) {
   auto kern = beam_search_warp_kernel<BWCAP, HBITS, MAXC, METRIC>;
@@ -935,47 +1360,64 @@ void launch_t(const SearchArgs& a, cudaStream_t stream) {
   while (wpb > 1 && per_warp * wpb > 200 * 1024) wpb--;
   if (per_warp * wpb > 220 * 1024) throw std::runtime_error("search: shared memory per query too large");
   const size_t smem = per_warp * wpb;
-  // The shared-memory opt-in and the occupancy query cost a few microseconds
-  // each, so they are cached per (instantiation, device).  The opt-in is a
-  // maximum: it is only ever raised, never lowered by a smaller launch, so a
-  // cached larger launch stays valid.
-  struct Launch { int sms, per_sm; };
-  static std::mutex m;
-  static std::map<std::pair<int, size_t>, Launch> cache;
-  static std::map<int, size_t> opted;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  Launch L{};
-  {
-    std::lock_guard<std::mutex> lock(m);
-    size_t& cur = opted[dev];
-    if (smem > cur) {
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-      cur = smem;
-    }
-    auto it = cache.find({dev, smem});
-    if (it != cache.end()) {
-      L = it->second;
-    } else {
-      cudaDeviceGetAttribute(&L.sms, cudaDevAttrMultiProcessorCount, dev);
-      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&L.per_sm, kern, 32 * wpb, smem);
-      if (L.per_sm < 1) L.per_sm = 1;
-      cache[{dev, smem}] = L;
-    }
-  }
-  const int sms = L.sms, per_sm = L.per_sm;
+  const LaunchShape L = launch_shape(kern, 32 * wpb, smem);
   const uint32_t need = (a.nq + wpb - 1) / wpb;
-  uint32_t grid = uint32_t(sms) * uint32_t(per_sm);
+  uint32_t grid = uint32_t(L.sms) * uint32_t(L.per_sm);
   if (grid > need) grid = need;
   if (grid == 0) return;
   kern<<<grid, 32 * wpb, smem, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) throw std::runtime_error(std::string("search launch: ") + cudaGetErrorString(e));
+  check_launch();
+}
+
+constexpr int kCtaWarps = 4;
+
+template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC>
+void launch_cta(const SearchArgs& a, cudaStream_t stream) {
+  auto kern = beam_search_cta_kernel<BWCAP, HBITS, MAXC, METRIC, kCtaWarps>;
+  const size_t smem =
+      warp_smem_bytes(BWCAP, HBITS, a.g.dpad, MAXC, a.rq_on ? 4 * ((a.g.dim + 31) / 32) : 0);
+  if (smem > 220 * 1024) throw std::runtime_error("search: shared memory per query too large");
+  const LaunchShape L = launch_shape(kern, 32 * kCtaWarps, smem);
+  uint32_t grid = uint32_t(L.sms) * uint32_t(L.per_sm);
+  if (grid > a.nq) grid = a.nq;
+  if (grid == 0) return;
+  kern<<<grid, 32 * kCtaWarps, smem, stream>>>(a);
+  check_launch();
+}
+
+// 0: choose per launch; 1: always a warp per query; 4: always a CTA per query.
+std::atomic<int> g_search_mode{0};
+
+#ifndef JB_CTA_QUERIES_PER_SM
+#define JB_CTA_QUERIES_PER_SM 12
+#endif
+// A CTA per query when the launch has fewer than this many queries per SM
+// (the warp-per-query kernel would leave most warp slots idle) and is a
+// query search (not the build's range search, which records expansions).
+bool use_cta(const SearchArgs& a) {
+  if (a.use_range || a.vis_idx != nullptr) return false;
+  const int mode = g_search_mode.load(std::memory_order_relaxed);
+  if (mode == 1) return false;
+  if (mode == 4) return true;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return a.nq < uint32_t(JB_CTA_QUERIES_PER_SM) * uint32_t(sms > 0 ? sms : 1);
 }
 
 template <uint32_t BWCAP, uint32_t HBITS>
 void dispatch_dim(const SearchArgs& a, cudaStream_t stream) {
   const uint32_t nchunks = a.g.dpad / 8;
+  if (use_cta(a)) {
+    // tile-of-4 layout for L2 rows up to 128 dims, the shared-memory query
+    // layout for everything else (same summation orders as the warp kernel)
+    if (a.g.metric == kIP) return launch_cta<BWCAP, HBITS, 0, kIP>(a, stream);
+    if (nchunks <= 4) return launch_cta<BWCAP, HBITS, 1, kL2>(a, stream);
+    if (nchunks <= 8) return launch_cta<BWCAP, HBITS, 2, kL2>(a, stream);
+    if (nchunks <= 12) return launch_cta<BWCAP, HBITS, 3, kL2>(a, stream);
+    if (nchunks <= 16) return launch_cta<BWCAP, HBITS, 4, kL2>(a, stream);
+    return launch_cta<BWCAP, HBITS, 0, kL2>(a, stream);
+  }
   if (a.g.metric == kIP) {
     if (nchunks <= 4) return launch_t<BWCAP, HBITS, 1, kIP>(a, stream);
     if (nchunks <= 8) return launch_t<BWCAP, HBITS, 2, kIP>(a, stream);
@@ -1004,6 +1446,12 @@ extern "C" int jb_debug_phase_clocks(unsigned long long* out, int reset) {
   return 0;
 }
 #endif
+
+void set_search_mode(int warps_per_query) {
+  if (warps_per_query != 0 && warps_per_query != 1 && warps_per_query != kCtaWarps)
+    throw std::invalid_argument("warps per query must be 0 (automatic), 1 or 4");
+  g_search_mode.store(warps_per_query, std::memory_order_relaxed);
+}
 
 void launch_search(const SearchArgs& a, cudaStream_t stream) {
   if (a.nq == 0) return;

@@ -17,6 +17,15 @@ from test_rabitq import golden_cases, regen, rotation, split
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=[1, 4], ids=["warp_per_query", "cta_per_query"], autouse=True)
+def kernel_mode(request, cuda):
+    """Every test runs on both query-search kernels (jb_search_set_warps_per_query)."""
+    from jasper_b200 import _lib
+    _lib.call("jb_search_set_warps_per_query", request.param)
+    yield request.param
+    _lib.call("jb_search_set_warps_per_query", 0)
+
+
 def device_quantize(X, c, metric, rot=None):
     import torch
     x = torch.from_numpy(np.ascontiguousarray(X, np.float32)).cuda()

@@ -14,6 +14,15 @@ import jb_testlib as T
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(params=[1, 4], ids=["warp_per_query", "cta_per_query"], autouse=True)
+def kernel_mode(request, cuda):
+    """Every test runs on both query-search kernels (jb_search_set_warps_per_query)."""
+    from jasper_b200 import _lib
+    _lib.call("jb_search_set_warps_per_query", request.param)
+    yield request.param
+    _lib.call("jb_search_set_warps_per_query", 0)
+
 _GRAPHS = {}
 
 
