@@ -58,11 +58,11 @@ const char* jb_last_error(void);
 int jb_abi_version(void);
 
 /* Process-wide choice of the query-search kernel (no reference counterpart;
- * results are identical either way): 0 = automatic -- one CTA of 4 warps per
- * query when a launch has fewer than 12 queries per SM (small batches, where
+ * results are identical either way): 0 = automatic -- one CTA of 2 warps per
+ * query when a launch has fewer than 8 queries per SM (small batches, where
  * a query's latency decides the time), else one warp per query; 1 = always a
- * warp per query; 4 = always a CTA of 4 warps per query.  For tests and
- * tuning.  Other values are rejected. */
+ * warp per query; 2 or more = always a CTA of 2 warps per query.  For tests
+ * and tuning.  Negative values are rejected. */
 int jb_search_set_warps_per_query(int32_t warps_per_query);
 
 /* Build a graph (reference: ConstructGraph_##id, ffi/jasper_ffi_common.cuh:

@@ -14,7 +14,8 @@
 //       s has d(c, s) * alpha < d(row, c), stop at R (construct.cuh:379-473);
 //   (d) reverse edges (target = new neighbour, sink = batch row) are sorted
 //       by (target, sink) and split into one group per target
-//       (fill_reverse_edges + thrust semisort, construct.cuh:475-558);
+//       (fill_reverse_edges + thrust semisort, construct.cuh:475-558; here a
+//       stable radix sort of our own on the target id);
 //   (e) for every target: existing edges plus the sinks with fresh distances,
 //       sorted, pruned again and written back (construct.cuh:560-741).
 //
@@ -32,7 +33,6 @@
 // (one cheap pass) and then the sinks in group order.  This code keeps exactly
 // that, deterministically: existing edges, then sinks in (target, sink) order
 // until the cap; the sinks past the cap are never evaluated.
-#include <cub/device/device_radix_sort.cuh>
 #include <algorithm>
 #include <cstdlib>
 #include <stdexcept>
@@ -693,6 +693,146 @@ __global__ void group_starts_kernel(const uint64_t* keys, size_t total, uint32_t
   }
 }
 
+// (d') The semisort: a stable LSD radix sort of the reverse pairs on their
+// target id alone.  The pairs are produced sink-major (pair b * R + e belongs
+// to batch row b), so among equal targets input order is already ascending
+// sink order, and a stable sort by target yields the (target, sink) order of
+// the reference's thrust sort (construct.cuh:832-879) exactly.  Targets are
+// taken relative to the graph's first id; empty slots (target 0xFFFFFFFF)
+// map to n and so sort after every real target.  8-bit digits: per pass a
+// per-block digit histogram, one exclusive scan over (digit, block), and a
+// stable scatter in which each warp ranks its keys round by round with
+// __match_any_sync.
+constexpr int kSortThreads = 256, kSortItems = 16, kSortTile = kSortThreads * kSortItems;
+constexpr int kSortWarps = kSortThreads / 32;
+
+__device__ __forceinline__ uint32_t sort_digit(uint64_t k, uint32_t first, uint32_t n, int shift) {
+  uint32_t t = uint32_t(k >> 32) - first;
+  if (t > n) t = n;
+  return (t >> shift) & 0xFFu;
+}
+
+__global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(const uint64_t* keys, size_t total,
+                                                                  uint32_t first, uint32_t n,
+                                                                  int shift, uint32_t* counts,
+                                                                  uint32_t nblocks) {
+  __shared__ uint32_t h[256];
+  for (int i = threadIdx.x; i < 256; i += kSortThreads) h[i] = 0;
+  __syncthreads();
+  const size_t base = size_t(blockIdx.x) * kSortTile;
+  for (int j = threadIdx.x; j < kSortTile; j += kSortThreads) {
+    const size_t i = base + j;
+    if (i < total) atomicAdd(&h[sort_digit(keys[i], first, n, shift)], 1u);
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < 256; d += kSortThreads) counts[size_t(d) * nblocks + blockIdx.x] = h[d];
+}
+
+// Exclusive prefix sum of a[0, len) in place, by one block of 1024 threads.
+__global__ void __launch_bounds__(1024) exclusive_scan_kernel(uint32_t* a, size_t len) {
+  __shared__ uint32_t wsum[32];
+  __shared__ uint32_t carry;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (size_t base = 0; base < len; base += 1024) {
+    const size_t i = base + threadIdx.x;
+    const uint32_t v = i < len ? a[i] : 0u;
+    uint32_t x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(kFull, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) wsum[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      uint32_t t = wsum[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(kFull, t, o);
+        if (lane >= o) t += y;
+      }
+      wsum[lane] = t;
+    }
+    __syncthreads();
+    const uint32_t before = carry + (w ? wsum[w - 1] : 0u);
+    if (i < len) a[i] = before + x - v;
+    __syncthreads();
+    if (threadIdx.x == 0) carry += wsum[31];
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(const uint64_t* in, uint64_t* out,
+                                                                     size_t total, uint32_t first,
+                                                                     uint32_t n, int shift,
+                                                                     const uint32_t* offsets,
+                                                                     uint32_t nblocks) {
+  __shared__ uint32_t wh[kSortWarps][256];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < kSortWarps * 256; i += kSortThreads) (&wh[0][0])[i] = 0;
+  __syncthreads();
+  // warp w holds keys [wbase, wbase + 32 * kSortItems) of the block's tile,
+  // round u covering 32 consecutive keys, so (warp, round, lane) is input order
+  const size_t wbase = size_t(blockIdx.x) * kSortTile + size_t(w) * 32 * kSortItems;
+  const uint32_t lt = (1u << lane) - 1u;
+  uint64_t key[kSortItems];
+  uint32_t rank[kSortItems];
+#pragma unroll
+  for (int u = 0; u < kSortItems; u++) {
+    const size_t i = wbase + size_t(u) * 32 + lane;
+    const bool valid = i < total;
+    key[u] = valid ? in[i] : 0ull;
+    const uint32_t d = valid ? sort_digit(key[u], first, n, shift) : 256u;
+    const uint32_t peers = __match_any_sync(kFull, d);
+    const uint32_t before = valid ? wh[w][d] : 0u;
+    __syncwarp();
+    if (valid && lane == __ffs(peers) - 1) wh[w][d] = before + __popc(peers);
+    __syncwarp();
+    rank[u] = before + __popc(peers & lt);
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < 256; d += kSortThreads) {  // warps in input order
+    uint32_t run = 0;
+#pragma unroll
+    for (int ww = 0; ww < kSortWarps; ww++) {
+      const uint32_t c = wh[ww][d];
+      wh[ww][d] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int u = 0; u < kSortItems; u++) {
+    const size_t i = wbase + size_t(u) * 32 + lane;
+    if (i < total) {
+      const uint32_t d = sort_digit(key[u], first, n, shift);
+      out[offsets[size_t(d) * nblocks + blockIdx.x] + wh[w][d] + rank[u]] = key[u];
+    }
+  }
+}
+
+// Sorts keys[0, total) (contents clobbered) using tmp; returns the buffer
+// holding the sorted keys.
+const uint64_t* sort_reverse_pairs(uint64_t* keys, uint64_t* tmp, size_t total, uint32_t first,
+                                   uint32_t n, uint32_t* counts, cudaStream_t st) {
+  if (total == 0) return keys;
+  const int bits = 32 - __builtin_clz(n | 1u);  // digits of 0 .. n
+  const int passes = (bits + 7) / 8;
+  const uint32_t nblocks = uint32_t((total + kSortTile - 1) / kSortTile);
+  uint64_t* src = keys;
+  uint64_t* dst = tmp;
+  for (int p = 0; p < passes; p++) {
+    radix_hist_kernel<<<nblocks, kSortThreads, 0, st>>>(src, total, first, n, 8 * p, counts, nblocks);
+    exclusive_scan_kernel<<<1, 1024, 0, st>>>(counts, size_t(256) * nblocks);
+    radix_scatter_kernel<<<nblocks, kSortThreads, 0, st>>>(src, dst, total, first, n, 8 * p, counts,
+                                                          nblocks);
+    uint64_t* t = src; src = dst; dst = t;
+  }
+  return src;
+}
+
 // (e) one warp per reverse-edge target.
 template <int MAXC, int METRIC, bool GRAM>
 __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const uint64_t* keys,
@@ -809,7 +949,7 @@ struct Kernels {
   }
   template <bool GRAM>
   static void reverse_launch(const GraphView& g, size_t total, const BuildWorkspace& ws,
-                             float alpha, cudaStream_t st) {
+                             const uint64_t* sorted, float alpha, cudaStream_t st) {
     const int warps = GRAM ? JB_GRAM_WARPS : 4;
     const size_t smem = (prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) +
                          (GRAM ? gram_warp_bytes(g.dpad) : 0)) * warps;
@@ -824,24 +964,25 @@ struct Kernels {
     const size_t need = (total + warps - 1) / warps;
     if (blocks > need) blocks = need;
     if (blocks == 0) blocks = 1;
-    k<<<uint32_t(blocks), 32 * warps, smem, st>>>(g, ws.rev_sorted, total, ws.group_starts,
+    k<<<uint32_t(blocks), 32 * warps, smem, st>>>(g, sorted, total, ws.group_starts,
                                                   ws.counters + 1, alpha);
   }
-  static void reverse(const GraphView& g, size_t total, const BuildWorkspace& ws, float alpha,
-                      cudaStream_t st) {
+  static void reverse(const GraphView& g, size_t total, const BuildWorkspace& ws,
+                      const uint64_t* sorted, float alpha, cudaStream_t st) {
     if (gram_prune_enabled() && g.dpad <= 128 && alpha > 0.f)
-      reverse_launch<true>(g, total, ws, alpha, st);
+      reverse_launch<true>(g, total, ws, sorted, alpha, st);
     else
-      reverse_launch<false>(g, total, ws, alpha, st);
+      reverse_launch<false>(g, total, ws, sorted, alpha, st);
   }
 };
 
 template <int METRIC>
 void dispatch_prune(const GraphView& g, uint32_t off, uint32_t bs, const BuildWorkspace& ws,
-                    float alpha, cudaStream_t st, bool reverse, size_t total) {
+                    float alpha, cudaStream_t st, bool reverse, size_t total,
+                    const uint64_t* sorted = nullptr) {
   const uint32_t nchunks = g.dim / 8;
   auto run = [&](auto kernels) {
-    if (reverse) decltype(kernels)::reverse(g, total, ws, alpha, st);
+    if (reverse) decltype(kernels)::reverse(g, total, ws, sorted, alpha, st);
     else decltype(kernels)::prune(g, off, bs, ws, alpha, st);
   };
   if (METRIC == kIP) return run(Kernels<0, METRIC>{});
@@ -886,10 +1027,8 @@ void workspace_allocate(BuildWorkspace& ws, uint32_t max_batch, uint32_t R) {
   check(cudaMalloc(&ws.rev_sorted, pairs * 8), "alloc sorted reverse pairs");
   check(cudaMalloc(&ws.group_starts, pairs * 4), "alloc group starts");
   check(cudaMalloc(&ws.counters, 256), "alloc counters");
-  size_t tmp = 0;
-  cub::DeviceRadixSort::SortKeys(nullptr, tmp, ws.rev_keys, ws.rev_sorted, int(pairs), 0, 64);
-  ws.sort_tmp_bytes = tmp;
-  check(cudaMalloc(&ws.sort_tmp, tmp ? tmp : 16), "alloc sort scratch");
+  ws.sort_tmp_bytes = size_t(256) * ((pairs + kSortTile - 1) / kSortTile) * 4;
+  check(cudaMalloc(&ws.sort_tmp, ws.sort_tmp_bytes ? ws.sort_tmp_bytes : 16), "alloc sort counts");
 }
 
 void workspace_free(BuildWorkspace& ws) {
@@ -922,13 +1061,11 @@ void process_batch(Graph& graph, BuildWorkspace& ws, uint32_t off, uint32_t bs, 
   const size_t total = size_t(bs) * g.R;
   const uint32_t fb = uint32_t(std::min<size_t>((total + 255) / 256, 4096));
   fill_reverse_kernel<<<fb, 256, 0, st>>>(g, off, bs, ws.rev_keys);
-  size_t tmp = ws.sort_tmp_bytes;
-  check(cub::DeviceRadixSort::SortKeys(ws.sort_tmp, tmp, ws.rev_keys, ws.rev_sorted, int(total), 0,
-                                       64, st),
-        "sort reverse pairs");
-  group_starts_kernel<<<fb, 256, 0, st>>>(ws.rev_sorted, total, ws.group_starts, ws.counters + 1);
-  if (g.metric == kIP) dispatch_prune<kIP>(g, off, bs, ws, alpha, st, true, total);
-  else dispatch_prune<kL2>(g, off, bs, ws, alpha, st, true, total);
+  const uint64_t* sorted = sort_reverse_pairs(ws.rev_keys, ws.rev_sorted, total, g.global_offset,
+                                              g.n, static_cast<uint32_t*>(ws.sort_tmp), st);
+  group_starts_kernel<<<fb, 256, 0, st>>>(sorted, total, ws.group_starts, ws.counters + 1);
+  if (g.metric == kIP) dispatch_prune<kIP>(g, off, bs, ws, alpha, st, true, total, sorted);
+  else dispatch_prune<kL2>(g, off, bs, ws, alpha, st, true, total, sorted);
   check(cudaGetLastError(), "construct batch launch");
 }
 

@@ -1010,7 +1010,7 @@ __device__ __forceinline__ void cta_smemq_rows(const WarpSmem& sm, const GraphVi
 // MAXC: 1..4 = tile-of-4 layout (L2, dpad <= 128); 0 = shared-memory query
 // (any dpad, L2 or inner product).
 template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC, int W>
-__global__ void __launch_bounds__(32 * W, 4) beam_search_cta_kernel(SearchArgs a) {
+__global__ void __launch_bounds__(32 * W, 16 / W) beam_search_cta_kernel(SearchArgs a) {
   constexpr bool kTile = MAXC > 0;
   extern __shared__ __align__(16) char smem_raw[];
   __shared__ uint32_t s_q, s_m, s_cnt, s_flip, s_first;
@@ -1369,7 +1369,10 @@ void launch_t(const SearchArgs& a, cudaStream_t stream) {
   check_launch();
 }
 
-constexpr int kCtaWarps = 4;
+#ifndef JB_CTA_WARPS
+#define JB_CTA_WARPS 2
+#endif
+constexpr int kCtaWarps = JB_CTA_WARPS;
 
 template <uint32_t BWCAP, uint32_t HBITS, int MAXC, int METRIC>
 void launch_cta(const SearchArgs& a, cudaStream_t stream) {
@@ -1385,11 +1388,12 @@ void launch_cta(const SearchArgs& a, cudaStream_t stream) {
   check_launch();
 }
 
-// 0: choose per launch; 1: always a warp per query; 4: always a CTA per query.
+// 0: choose per launch; 1: always a warp per query; 2 or more: always a CTA
+// (of kCtaWarps warps) per query.
 std::atomic<int> g_search_mode{0};
 
 #ifndef JB_CTA_QUERIES_PER_SM
-#define JB_CTA_QUERIES_PER_SM 12
+#define JB_CTA_QUERIES_PER_SM 8
 #endif
 // A CTA per query when the launch has fewer than this many queries per SM
 // (the warp-per-query kernel would leave most warp slots idle) and is a
@@ -1398,7 +1402,7 @@ bool use_cta(const SearchArgs& a) {
   if (a.use_range || a.vis_idx != nullptr) return false;
   const int mode = g_search_mode.load(std::memory_order_relaxed);
   if (mode == 1) return false;
-  if (mode == 4) return true;
+  if (mode >= 2) return true;
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1448,9 +1452,8 @@ extern "C" int jb_debug_phase_clocks(unsigned long long* out, int reset) {
 #endif
 
 void set_search_mode(int warps_per_query) {
-  if (warps_per_query != 0 && warps_per_query != 1 && warps_per_query != kCtaWarps)
-    throw std::invalid_argument("warps per query must be 0 (automatic), 1 or 4");
-  g_search_mode.store(warps_per_query, std::memory_order_relaxed);
+  if (warps_per_query < 0) throw std::invalid_argument("warps per query must be >= 0");
+  g_search_mode.store(warps_per_query >= 2 ? kCtaWarps : warps_per_query, std::memory_order_relaxed);
 }
 
 void launch_search(const SearchArgs& a, cudaStream_t stream) {

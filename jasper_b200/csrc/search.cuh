@@ -52,9 +52,9 @@ constexpr size_t kSearchScratchBytes = 256;
 // memory (the caller clears it on the same stream).  Throws on bad arguments.
 void launch_search(const SearchArgs& a, cudaStream_t stream);
 
-// Process-wide kernel choice for query searches: 0 = automatic (a CTA of 4
-// warps per query when a launch has few queries per SM, else a warp per
-// query), 1 = always a warp per query, 4 = always a CTA per query.
+// Process-wide kernel choice for query searches: 0 = automatic (a CTA of 2
+// warps per query when a launch has fewer than 8 queries per SM, else a warp
+// per query), 1 = always a warp per query, 2 or more = always a CTA per query.
 void set_search_mode(int warps_per_query);
 
 // Number of kernel launches launch_search issues (for launch accounting).

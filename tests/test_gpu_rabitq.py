@@ -19,7 +19,8 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(params=[1, 4], ids=["warp_per_query", "cta_per_query"], autouse=True)
 def kernel_mode(request, cuda):
-    """Every test runs on both query-search kernels (jb_search_set_warps_per_query)."""
+    """Every test runs on both query-search kernels (jb_search_set_warps_per_query:
+    1 = a warp per query, 4 = a CTA per query)."""
     from jasper_b200 import _lib
     _lib.call("jb_search_set_warps_per_query", request.param)
     yield request.param
