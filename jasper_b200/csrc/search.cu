@@ -395,6 +395,18 @@ __device__ __forceinline__ float2 tile4_pair_sum(float2 v) {
   return __fadd2_rn(v, w);
 }
 
+#ifndef JB_MIXED_ADD
+#define JB_MIXED_ADD 0
+#endif
+// fl(f32(h) + c) for the fp16 value in the low half of w: add.rn.f32.f16
+// widens h exactly, then adds and rounds in fp32.
+__device__ __forceinline__ float add_f32_f16(uint32_t w, float c) {
+  float d;
+  const unsigned short h = static_cast<unsigned short>(w & 0xFFFFu);
+  asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(d) : "h"(h), "f"(c));
+  return d;
+}
+
 template <int NQ>
 __device__ __forceinline__ float2 tile4_pair_chain(const float* qs, const uint4 (&ua)[NQ],
                                                    const uint4 (&ub)[NQ]) {
@@ -408,11 +420,21 @@ __device__ __forceinline__ float2 tile4_pair_chain(const float* qs, const uint4 
     const uint32_t bw[4] = {ub[k].x, ub[k].y, ub[k].z, ub[k].w};
 #pragma unroll
     for (int w = 0; w < 4; w++) {
+#if JB_MIXED_ADD
+      // x + (-q) with the fp16 row element widened inside the add (exact, so
+      // the same bits as converting first): one instruction per element.
+      const float2 d0 = make_float2(add_f32_f16(aw[w], qv[2 * w]), add_f32_f16(bw[w], qv[2 * w]));
+      acc = __ffma2_rn(d0, d0, acc);
+      const float2 d1 = make_float2(add_f32_f16(aw[w] >> 16, qv[2 * w + 1]),
+                                    add_f32_f16(bw[w] >> 16, qv[2 * w + 1]));
+      acc = __ffma2_rn(d1, d1, acc);
+#else
       const float2 fa = h2f(aw[w]), fb = h2f(bw[w]);
       const float2 d0 = __fadd2_rn(make_float2(fa.x, fb.x), make_float2(qv[2 * w], qv[2 * w]));
       acc = __ffma2_rn(d0, d0, acc);
       const float2 d1 = __fadd2_rn(make_float2(fa.y, fb.y), make_float2(qv[2 * w + 1], qv[2 * w + 1]));
       acc = __ffma2_rn(d1, d1, acc);
+#endif
     }
   }
   return acc;

@@ -32,7 +32,33 @@ CASES = [
     # threshold: exercises the exact fallback of the Gram-filtered prune
     ("dup_sift", 4000, 128, 32, 0, 1.2),
     ("dup_sift", 3000, 64, 16, 1, 1.0),
+    # rows near the fp16 limit, large-norm near-duplicates and three scales
+    # in one candidate list: where the Gram filter's error band is thinnest
+    ("adversarial", 3000, 128, 32, 0, 1.2),
+    ("adversarial", 2000, 64, 16, 1, 1.0),
 ]
+
+
+def adversarial(n, dim, seed):
+    """Thirds of the rows at three scales: uniform in +-60000 (squared
+    norms near 4.6e11 at 128 dims), in +-64 and in +-0.01; a quarter of the
+    rows are near-duplicates of another row of their scale (a few
+    coordinates moved by one or two fp16 steps), in shuffled order."""
+    rng = np.random.default_rng(seed)
+    scales = np.array([60000.0, 64.0, 0.01])
+    X = (rng.uniform(-1.0, 1.0, size=(n, dim)) * scales[np.arange(n) % 3, None]).astype(np.float16)
+    dup = rng.random(n) < 0.25
+    src = rng.integers(0, n, size=n)
+    src = src - (src % 3) + (np.arange(n) % 3)          # same scale as the copy
+    src = np.minimum(src, n - 1)
+    X[dup] = X[src[dup]]
+    bits = X.view(np.uint16)
+    for i in np.flatnonzero(dup):
+        cols = rng.integers(0, dim, size=3)
+        bits[i, cols] = bits[i, cols] + rng.integers(1, 3, size=3).astype(np.uint16)
+    X = bits.view(np.float16)
+    assert np.isfinite(X.astype(np.float32)).all()
+    return X[rng.permutation(n)]
 
 
 def dup_sift(n, dim, seed):
@@ -58,7 +84,12 @@ def assert_graph_equal(e, d, c, g, msg=""):
 @pytest.mark.parametrize("case", CASES, ids=lambda c: f"{c[0]}-n{c[1]}-d{c[2]}-R{c[3]}-m{c[4]}")
 def test_build_matches_oracle(cuda, case):
     kind, n, dim, R, metric, alpha = case
-    X = dup_sift(n, dim, 31) if kind == "dup_sift" else getattr(synthetic, kind)(n, dim, 31)
+    if kind == "dup_sift":
+        X = dup_sift(n, dim, 31)
+    elif kind == "adversarial":
+        X = adversarial(n, dim, 31)
+    else:
+        X = getattr(synthetic, kind)(n, dim, 31)
     budget = 10 * 10**9
     g = O.OracleGraph(X, R, metric=metric)
     g.build(alpha, max(1, O.reference_max_batch_size(budget, n, R)))
