@@ -324,12 +324,19 @@ __device__ __forceinline__ float row_dist_lane(const float2* qp, const uint4* ro
           const uint32_t bw[4] = {ub.x, ub.y, ub.z, ub.w};
 #pragma unroll
           for (int w = 0; w < 4; w++) {
-            const float2 fa = h2f(aw[w]), fb = h2f(bw[w]);
             const float4 q2 = *reinterpret_cast<const float4*>(qq + 2 * w);
+#if JB_MIXED_ADD
+            float2 d0 = make_float2(add_f32_f16(aw[w], q2.x), add_f32_f16(bw[w], q2.y));
+            acc = __ffma2_rn(d0, d0, acc);
+            float2 d1 = make_float2(add_f32_f16(aw[w] >> 16, q2.z), add_f32_f16(bw[w] >> 16, q2.w));
+            acc = __ffma2_rn(d1, d1, acc);
+#else
+            const float2 fa = h2f(aw[w]), fb = h2f(bw[w]);
             float2 d0 = __fadd2_rn(make_float2(fa.x, fb.x), make_float2(q2.x, q2.y));
             acc = __ffma2_rn(d0, d0, acc);
             float2 d1 = __fadd2_rn(make_float2(fa.y, fb.y), make_float2(q2.z, q2.w));
             acc = __ffma2_rn(d1, d1, acc);
+#endif
           }
         }
       }
@@ -393,18 +400,6 @@ __device__ __forceinline__ float2 tile4_pair_sum(float2 v) {
   v = __fadd2_rn(v, w);
   w = make_float2(__shfl_xor_sync(kFull, v.x, 1), __shfl_xor_sync(kFull, v.y, 1));
   return __fadd2_rn(v, w);
-}
-
-#ifndef JB_MIXED_ADD
-#define JB_MIXED_ADD 0
-#endif
-// fl(f32(h) + c) for the fp16 value in the low half of w: add.rn.f32.f16
-// widens h exactly, then adds and rounds in fp32.
-__device__ __forceinline__ float add_f32_f16(uint32_t w, float c) {
-  float d;
-  const unsigned short h = static_cast<unsigned short>(w & 0xFFFFu);
-  asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(d) : "h"(h), "f"(c));
-  return d;
 }
 
 template <int NQ>
