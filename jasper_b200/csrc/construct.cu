@@ -700,9 +700,9 @@ __global__ void group_starts_kernel(const uint64_t* keys, size_t total, uint32_t
 // the reference's thrust sort (construct.cuh:832-879) exactly.  Targets are
 // taken relative to the graph's first id; empty slots (target 0xFFFFFFFF)
 // map to n and so sort after every real target.  8-bit digits: per pass a
-// per-block digit histogram, one exclusive scan over (digit, block), and a
-// stable scatter in which each warp ranks its keys round by round with
-// __match_any_sync.
+// per-block digit histogram, an exclusive scan of every digit's row of block
+// counts (one block per digit), and a stable scatter that adds the digits'
+// bases and ranks each warp's keys round by round with __match_any_sync.
 constexpr int kSortThreads = 256, kSortItems = 16, kSortTile = kSortThreads * kSortItems;
 constexpr int kSortWarps = kSortThreads / 32;
 
@@ -728,16 +728,19 @@ __global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(const uint64_t
   for (int d = threadIdx.x; d < 256; d += kSortThreads) counts[size_t(d) * nblocks + blockIdx.x] = h[d];
 }
 
-// Exclusive prefix sum of a[0, len) in place, by one block of 1024 threads.
-__global__ void __launch_bounds__(1024) exclusive_scan_kernel(uint32_t* a, size_t len) {
+// Exclusive prefix sum of digit d's row counts[d][0, nblocks) in place, one
+// block per digit; the row total goes to totals[d].
+__global__ void __launch_bounds__(1024) digit_rows_scan_kernel(uint32_t* counts, uint32_t nblocks,
+                                                               uint32_t* totals) {
   __shared__ uint32_t wsum[32];
   __shared__ uint32_t carry;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  uint32_t* a = counts + size_t(blockIdx.x) * nblocks;
   if (threadIdx.x == 0) carry = 0;
   __syncthreads();
-  for (size_t base = 0; base < len; base += 1024) {
-    const size_t i = base + threadIdx.x;
-    const uint32_t v = i < len ? a[i] : 0u;
+  for (uint32_t base = 0; base < nblocks; base += 1024) {
+    const uint32_t i = base + threadIdx.x;
+    const uint32_t v = i < nblocks ? a[i] : 0u;
     uint32_t x = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -757,21 +760,38 @@ __global__ void __launch_bounds__(1024) exclusive_scan_kernel(uint32_t* a, size_
     }
     __syncthreads();
     const uint32_t before = carry + (w ? wsum[w - 1] : 0u);
-    if (i < len) a[i] = before + x - v;
+    if (i < nblocks) a[i] = before + x - v;
     __syncthreads();
     if (threadIdx.x == 0) carry += wsum[31];
     __syncthreads();
   }
+  if (threadIdx.x == 0) totals[blockIdx.x] = carry;
 }
 
 __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(const uint64_t* in, uint64_t* out,
                                                                      size_t total, uint32_t first,
                                                                      uint32_t n, int shift,
                                                                      const uint32_t* offsets,
-                                                                     uint32_t nblocks) {
+                                                                     uint32_t nblocks,
+                                                                     const uint32_t* totals) {
   __shared__ uint32_t wh[kSortWarps][256];
+  __shared__ uint32_t digit_base[256];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < kSortWarps * 256; i += kSortThreads) (&wh[0][0])[i] = 0;
+  if (w == 0) {  // exclusive prefix of the 256 digit totals, 8 per lane
+    uint32_t v[8], run = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) { v[j] = totals[8 * lane + j]; run += v[j]; }
+    uint32_t x = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(kFull, x, o);
+      if (lane >= o) x += y;
+    }
+    uint32_t b = x - run;
+#pragma unroll
+    for (int j = 0; j < 8; j++) { digit_base[8 * lane + j] = b; b += v[j]; }
+  }
   __syncthreads();
   // warp w holds keys [wbase, wbase + 32 * kSortItems) of the block's tile,
   // round u covering 32 consecutive keys, so (warp, round, lane) is input order
@@ -808,7 +828,7 @@ __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(const uint6
     const size_t i = wbase + size_t(u) * 32 + lane;
     if (i < total) {
       const uint32_t d = sort_digit(key[u], first, n, shift);
-      out[offsets[size_t(d) * nblocks + blockIdx.x] + wh[w][d] + rank[u]] = key[u];
+      out[digit_base[d] + offsets[size_t(d) * nblocks + blockIdx.x] + wh[w][d] + rank[u]] = key[u];
     }
   }
 }
@@ -825,9 +845,9 @@ const uint64_t* sort_reverse_pairs(uint64_t* keys, uint64_t* tmp, size_t total, 
   uint64_t* dst = tmp;
   for (int p = 0; p < passes; p++) {
     radix_hist_kernel<<<nblocks, kSortThreads, 0, st>>>(src, total, first, n, 8 * p, counts, nblocks);
-    exclusive_scan_kernel<<<1, 1024, 0, st>>>(counts, size_t(256) * nblocks);
+    digit_rows_scan_kernel<<<256, 1024, 0, st>>>(counts, nblocks, counts + size_t(256) * nblocks);
     radix_scatter_kernel<<<nblocks, kSortThreads, 0, st>>>(src, dst, total, first, n, 8 * p, counts,
-                                                          nblocks);
+                                                          nblocks, counts + size_t(256) * nblocks);
     uint64_t* t = src; src = dst; dst = t;
   }
   return src;
@@ -1027,7 +1047,7 @@ void workspace_allocate(BuildWorkspace& ws, uint32_t max_batch, uint32_t R) {
   check(cudaMalloc(&ws.rev_sorted, pairs * 8), "alloc sorted reverse pairs");
   check(cudaMalloc(&ws.group_starts, pairs * 4), "alloc group starts");
   check(cudaMalloc(&ws.counters, 256), "alloc counters");
-  ws.sort_tmp_bytes = size_t(256) * ((pairs + kSortTile - 1) / kSortTile) * 4;
+  ws.sort_tmp_bytes = size_t(256) * ((pairs + kSortTile - 1) / kSortTile + 1) * 4;
   check(cudaMalloc(&ws.sort_tmp, ws.sort_tmp_bytes ? ws.sort_tmp_bytes : 16), "alloc sort counts");
 }
 

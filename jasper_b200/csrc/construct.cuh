@@ -21,7 +21,7 @@ struct BuildWorkspace {
   uint64_t* rev_sorted = nullptr;  // [max_batch * R]
   uint32_t* group_starts = nullptr;
   uint32_t* counters = nullptr;    // [0] search work counter, [1] reverse group count
-  void* sort_tmp = nullptr;        // semisort digit counts: [256][blocks of 4096 pairs]
+  void* sort_tmp = nullptr;        // semisort counts: [256][blocks of 4096 pairs], then 256 totals
   size_t sort_tmp_bytes = 0;
 };
 
