@@ -471,6 +471,10 @@ int jb_graph_set_edges(int64_t handle, const uint32_t* edges, const uint16_t* ed
     cuda_check(cudaMemcpy(g->edist, edge_dists, nr * 2, cudaMemcpyDefault), "set dists");
     cuda_check(cudaMemcpy(g->counts, counts, g->n, cudaMemcpyDefault), "set counts");
     g->medoid = medoid;
+    if (g->eflag) {  // edges set from outside: no prune of them is known
+      cudaFree(g->eflag);
+      g->eflag = nullptr;
+    }
   });
 }
 

@@ -196,7 +196,7 @@ constexpr int kPruneGroup = 8;
 #endif
 
 #ifdef JB_BUILD_CLOCKS
-__device__ unsigned long long g_build_clk[4];
+__device__ unsigned long long g_build_clk[8];
 #endif  // candidates tested at once, one per 4-lane tile
 
 // The kept-row cache is used where the candidate row sits in registers (L2,
@@ -222,6 +222,34 @@ __device__ __forceinline__ PruneSmem prune_carve(char* base, uint32_t dpad) {
   p.selrows = reinterpret_cast<uint4*>(reinterpret_cast<char*>(p.row) +
                                        ((size_t(dpad) * 2 + 15) & ~size_t(15)));
   return p;
+}
+
+// Write the kept list sm.sel / sm.sel_d (ns entries) as the row of `self`:
+// ids, bf16 distances, count and, when the build keeps them, the prune flags
+// (bit i: the distance kept slot i was tested with is exactly its stored
+// bf16 value).
+__device__ __forceinline__ void write_pruned_row(const GraphView& g, uint32_t self,
+                                                 const PruneSmem& sm, uint32_t ns, int lane) {
+  const uint32_t l = self - g.global_offset;
+  const uint32_t R = g.R;
+  uint64_t mask = 0;
+  for (uint32_t i0 = 0; i0 < ns; i0 += 32) {
+    const uint32_t i = i0 + lane;
+    bool exact = false;
+    if (i < ns) {
+      const float d = sm.sel_d[i];
+      const uint16_t b = float_to_bf16_bits(d);
+      g.edges[size_t(l) * R + i] = sm.sel[i];
+      g.edist[size_t(l) * R + i] = b;
+      exact = bf16_bits_to_float(b) == d;
+    }
+    mask |= uint64_t(__ballot_sync(kFull, exact)) << i0;
+  }
+  if (lane == 0) {
+    g.counts[l] = uint8_t(ns);
+    if (g.eflag != nullptr) g.eflag[l] = mask;
+  }
+  __syncwarp();
 }
 
 // Sort cand[0, nc) ascending (pads the power-of-two tail with the max key).
@@ -386,13 +414,194 @@ __device__ void prune_and_write(const GraphView& gv, uint32_t self, PruneSmem& s
     }
   }
   __syncwarp();
-  const uint32_t l = self - g.global_offset;
-  for (uint32_t i = lane; i < ns; i += 32) {
-    g.edges[size_t(l) * R + i] = sm.sel[i];
-    g.edist[size_t(l) * R + i] = float_to_bf16_bits(sm.sel_d[i]);
+  write_pruned_row(g, self, sm, ns, lane);
+}
+
+// ---------------------------------------------------------------------------
+// Incremental RobustPrune for one reverse-edge target.
+//
+// A kept edge is "trusted" (GraphView::eflag) when the prune that kept it
+// tested it with exactly the distance now stored for it (the bf16 value):
+// every existing edge a re-prune kept, and every new candidate whose fp32
+// distance is exact in bf16.  For two trusted edges a before b nothing about
+// their test has changed since b was kept: same keys, so the same relative
+// order; same distances; and b passed against every kept row before it,
+// a among them.  So in a re-prune a trusted b can only be pruned by an
+// untrusted kept candidate before it (a new sink, or an edge whose test used
+// its unrounded distance), and untrusted candidates need the full test.
+// This path computes only the distances between the untrusted candidates and
+// all others (the pair distance is symmetric bit for bit: (x - y)^2 and
+// x * y are), then walks the sorted list exactly like prune_and_write, so
+// the kept list is the one the full walk keeps.
+// Used when at most kIncrMaxNew candidates are untrusted and nc <= 96; the
+// distances live in the unused tail of sm.cand ([kIncrMaxNew][96] floats).
+// ---------------------------------------------------------------------------
+#ifndef JB_INCR_MAX_NEW
+#define JB_INCR_MAX_NEW 8
+#endif
+constexpr int kIncrMaxNew = JB_INCR_MAX_NEW;
+constexpr int kIncrMaxCand = 96;
+
+// Scratch (inside the Gram scratch of the warp): the existing edges' keys
+// before the sort, the untrusted candidates' rows, their distances.
+struct IncrScratch {
+  uint64_t* oldkeys;  // [64]
+  uint4* nrows;       // [kIncrMaxNew][dpad / 8]
+  float* dn;          // [kIncrMaxNew][kIncrMaxCand]
+};
+__host__ __device__ inline size_t incr_scratch_bytes(uint32_t dpad) {
+  return 64 * 8 + size_t(kIncrMaxNew) * dpad * 2 + size_t(kIncrMaxNew) * kIncrMaxCand * 4;
+}
+__device__ __forceinline__ IncrScratch incr_carve(char* base, uint32_t dpad) {
+  IncrScratch x;
+  x.oldkeys = reinterpret_cast<uint64_t*>(base);
+  x.nrows = reinterpret_cast<uint4*>(x.oldkeys + 64);
+  x.dn = reinterpret_cast<float*>(reinterpret_cast<char*>(x.nrows) + size_t(kIncrMaxNew) * dpad * 2);
+  return x;
+}
+
+// L2 with the candidate rows in registers (MAXC chunks per lane) only.
+// oldtrust: bit a = existing edge a (x.oldkeys[a], a < na) is trusted.
+template <int MAXC>
+__device__ bool incremental_prune_and_write(const GraphView& g, uint32_t self, PruneSmem& sm,
+                                            const IncrScratch& x, int na, int nc, float alpha,
+                                            int lane, uint64_t oldtrust) {
+  if (nc > kIncrMaxCand) return false;
+  const int tile = lane >> 2, s = lane & 3;
+  const int nchunks = int(g.dim / 8);
+  const int stride = int(g.dpad / 8);
+  // trusted positions: candidates whose key is a trusted existing edge's
+  uint64_t t0 = 0, t1 = 0;
+  for (int p0 = 0; p0 < nc; p0 += 32) {
+    const int p = p0 + lane;
+    bool tr = false;
+    if (p < nc) {
+      const uint64_t key = sm.cand[p];
+      // a key present twice (an existing edge again as a sink) is trusted
+      // at its first position only: the second is tested like a new one
+      if (p == 0 || sm.cand[p - 1] != key)
+        for (int j = 0; j < na; j++)
+          if (x.oldkeys[j] == key) { tr = (oldtrust >> j) & 1ull; break; }
+    }
+    const uint64_t b = __ballot_sync(kFull, tr);
+    if (p0 < 64) t0 |= b << p0; else t1 |= b << (p0 - 64);
   }
-  if (lane == 0) g.counts[l] = uint8_t(ns);
+  const uint64_t u0 = ~t0 & (nc >= 64 ? ~0ull : ((1ull << nc) - 1ull));
+  const uint64_t u1 = nc > 64 ? (~t1 & ((1ull << (nc - 64)) - 1ull)) : 0ull;
+  const int nn = __popcll(u0) + __popcll(u1);
+  if (nn > kIncrMaxNew) return false;
+  // positions of the untrusted candidates, in order (the keys are no longer
+  // needed: their slots hold the positions)
+  int* upos = reinterpret_cast<int*>(x.oldkeys);
   __syncwarp();
+  if (lane == 0) {
+    uint64_t a = u0, b = u1;
+    for (int k = 0; k < nn; k++) {
+      if (a) { upos[k] = __ffsll(static_cast<long long>(a)) - 1; a &= a - 1; }
+      else { upos[k] = 64 + __ffsll(static_cast<long long>(b)) - 1; b &= b - 1; }
+    }
+  }
+  __syncwarp();
+  // stage the untrusted rows
+  for (int k = 0; k < nn; k++) {
+    const int pk = upos[k];
+    const uint4* row = reinterpret_cast<const uint4*>(
+        g.vec + size_t(pair_id(sm.cand[pk]) - g.global_offset) * g.dpad);
+    for (int c = lane; c < stride; c += 32) x.nrows[k * stride + c] = ldg16(row + c);
+  }
+  __syncwarp();
+  // d(untrusted k, candidate j): each tile holds two candidate rows and runs
+  // them against every staged row -- RowReg::dist's chunks and order
+  for (int base = 0; base < nc; base += 16) {
+    int jj[2];
+    uint4 u[2][MAXC];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      jj[h] = base + tile + 8 * h;
+      const bool act = jj[h] < nc;
+      const uint4* row = reinterpret_cast<const uint4*>(
+          g.vec + size_t(act ? pair_id(sm.cand[jj[h]]) - g.global_offset : 0) * g.dpad);
+#pragma unroll
+      for (int i = 0; i < MAXC; i++) {
+        const int c = s + 4 * i;
+        u[h][i] = (act && c < nchunks) ? ldg16(row + c) : make_uint4(0, 0, 0, 0);
+      }
+    }
+    for (int k = 0; k < nn; k++) {
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < MAXC; i++) {
+          const int c = s + 4 * i;
+          if (c < nchunks) acc = l2_chunk(u[h][i], x.nrows[k * stride + c], acc);
+        }
+        acc = tile4_sum(acc);
+        if (s == 0 && jj[h] < nc) x.dn[k * kIncrMaxCand + jj[h]] = acc;
+      }
+    }
+  }
+  __syncwarp();
+  // The walk of prune_and_write.  Between two untrusted candidates every
+  // trusted one depends only on the untrusted candidates kept before it, so
+  // a run of trusted candidates is decided at once; each untrusted candidate
+  // is tested against everything kept before it.  The cap R keeps the first
+  // R kept candidates.
+  const uint32_t R = g.R;
+  uint32_t ns = 0;
+  uint64_t k0 = 0, k1 = 0;  // kept positions
+  int lo = 0;               // first undecided position
+  for (int k = 0; k <= nn && ns < R; k++) {
+    const int hi = k < nn ? upos[k] : nc;  // next untrusted position
+    // trusted run [lo, hi)
+    for (int p0 = lo; p0 < hi && ns < R; p0 += 32) {
+      const int p = p0 + lane;
+      bool keep = false;
+      if (p < hi) {
+        const float cd = key_dist(sm.cand[p]);
+        keep = true;
+        for (int m = 0; m < k; m++) {
+          const int pm = upos[m];
+          const bool km = pm < 64 ? ((k0 >> pm) & 1ull) : ((k1 >> (pm - 64)) & 1ull);
+          if (km && x.dn[m * kIncrMaxCand + p] * alpha < cd) keep = false;
+        }
+      }
+      uint32_t bal = __ballot_sync(kFull, keep);
+      const uint32_t room = R - ns;
+      if (uint32_t(__popc(bal)) > room) {  // the walk stops at the R-th kept
+        for (uint32_t r = uint32_t(__popc(bal)); r > room; r--) bal &= ~(1u << (31 - __clz(bal)));
+      }
+      if ((bal >> lane) & 1u) {
+        const int slot = int(ns) + __popc(bal & ((1u << lane) - 1u));
+        sm.sel[slot] = pair_id(sm.cand[p]);
+        sm.sel_d[slot] = key_dist(sm.cand[p]);
+      }
+      const uint64_t wb = uint64_t(bal);
+      if (p0 < 64) { k0 |= wb << p0; if (p0 > 32) k1 |= wb >> (64 - p0); }
+      else k1 |= wb << (p0 - 64);
+      ns += __popc(bal);
+    }
+    if (k == nn || ns >= R) break;
+    // untrusted candidate at hi: every kept candidate before it
+    const float cd = key_dist(sm.cand[hi]);
+    bool p = false;
+    for (int j = lane; j < hi; j += 32) {
+      const bool kj = j < 64 ? ((k0 >> j) & 1ull) : ((k1 >> (j - 64)) & 1ull);
+      if (kj && x.dn[k * kIncrMaxCand + j] * alpha < cd) p = true;
+    }
+    if (!__any_sync(kFull, p)) {
+      if (lane == 0) {
+        sm.sel[ns] = pair_id(sm.cand[hi]);
+        sm.sel_d[ns] = cd;
+      }
+      if (hi < 64) k0 |= 1ull << hi; else k1 |= 1ull << (hi - 64);
+      ns++;
+    }
+    lo = hi + 1;
+  }
+  __syncwarp();
+  write_pruned_row(g, self, sm, ns, lane);
+  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -616,13 +825,8 @@ __device__ void gram_prune_and_write(const GraphView& g, uint32_t self, PruneSme
     }
     __syncwarp();
   }
-  const uint32_t l = self - g.global_offset;
-  for (uint32_t i = lane; i < ns; i += 32) {
-    g.edges[size_t(l) * R + i] = sm.sel[i];
-    g.edist[size_t(l) * R + i] = float_to_bf16_bits(sm.sel_d[i]);
-  }
-  if (lane == 0) g.counts[l] = uint8_t(ns);
   __syncwarp();
+  write_pruned_row(g, self, sm, ns, lane);
 }
 
 // (b) + (c) for batch rows [off, off + bs).
@@ -854,37 +1058,55 @@ const uint64_t* sort_reverse_pairs(uint64_t* keys, uint64_t* tmp, size_t total, 
 }
 
 // (e) one warp per reverse-edge target.
-template <int MAXC, int METRIC, bool GRAM>
+// PASS 0: every target group, one kernel (incremental prune when GRAM
+//         applies to L2 register rows, else the Gram / plain prune);
+// PASS 1: every group, incremental prune only: a group it cannot take is
+//         appended to `deferred`.  No Gram scratch, so several times the
+//         warps fit per SM;
+// PASS 2: the deferred groups, Gram / plain prune.
+template <int MAXC, int METRIC, bool GRAM, int PASS>
 __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const uint64_t* keys,
                                                             size_t total, const uint32_t* starts,
-                                                            const uint32_t* n_groups, float alpha) {
+                                                            const uint32_t* n_groups, float alpha,
+                                                            uint32_t* deferred,
+                                                            uint32_t* n_deferred) {
   extern __shared__ __align__(16) char smem_raw[];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int tile = lane >> 2, s = lane & 3;
   const size_t wbytes = prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on);
-  const size_t gbytes = GRAM ? gram_warp_bytes(g.dpad) : 0;
+  const size_t gbytes = PASS == 1 ? incr_scratch_bytes(g.dpad) : (GRAM ? gram_warp_bytes(g.dpad) : 0);
   char* wbase = smem_raw + (wbytes + gbytes) * wid;
   PruneSmem sm = prune_carve(wbase, g.dpad);
   const uint32_t R = g.R;
   const uint32_t cap = 256 + R;  // MAX_CANDS of construct.cuh:574
-  const uint32_t ng = *n_groups;
+  const uint32_t ng = PASS == 2 ? *n_deferred : *n_groups;
   const uint32_t nwarps = gridDim.x * (blockDim.x >> 5);
   const int nchunks = int(g.dim / 8);
-  for (uint32_t gi = blockIdx.x * (blockDim.x >> 5) + wid; gi < ng; gi += nwarps) {
+  for (uint32_t gw = blockIdx.x * (blockDim.x >> 5) + wid; gw < ng; gw += nwarps) {
+    const uint32_t gi = PASS == 2 ? deferred[gw] : gw;
     const size_t start = starts[gi];
     const uint32_t t = uint32_t(keys[start] >> 32);
     const uint32_t l = t - g.global_offset;
     int nc = 0;
     const uint32_t ne = g.counts[l];
+    constexpr bool kIncr = (PASS == 1) || (PASS == 0 && GRAM && MAXC > 0 && METRIC == kL2);
+    const uint64_t rowflags = (kIncr && g.eflag != nullptr) ? g.eflag[l] : 0ull;
+    uint64_t oldtrust = 0;  // trusted existing edges by index in cand
     for (uint32_t base = 0; base < ne; base += 32) {
       const uint32_t e = base + lane;
       uint32_t id = e < ne ? g.edges[size_t(l) * R + e] : kInvalid;
       const bool ok = e < ne && id != kInvalid;
       const uint32_t bal = __ballot_sync(kFull, ok);
-      if (ok) sm.cand[nc + __popc(bal & ((1u << lane) - 1u))] =
-          make_pair_key(bf16_bits_to_float(g.edist[size_t(l) * R + e]), id);
+      const int p = nc + __popc(bal & ((1u << lane) - 1u));
+      if (ok) sm.cand[p] = make_pair_key(bf16_bits_to_float(g.edist[size_t(l) * R + e]), id);
+      if (ok && ((rowflags >> e) & 1ull) && p < 64) oldtrust |= 1ull << p;
       nc += __popc(bal);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) oldtrust |= __shfl_xor_sync(kFull, oldtrust, o);
+    const IncrScratch incr = incr_carve(wbase + wbytes, g.dpad);
+    if (kIncr && oldtrust != 0)
+      for (int i = lane; i < nc; i += 32) incr.oldkeys[i] = sm.cand[i];
 #ifdef JB_BUILD_CLOCKS
     long long _c0 = clock64();
 #endif
@@ -931,8 +1153,22 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
 #ifdef JB_BUILD_CLOCKS
     long long _c2 = clock64();
 #endif
-    if (GRAM && nc <= kGramMax) gram_prune_and_write<METRIC>(g, t, sm, wbase + wbytes, nc, alpha, lane);
-    else prune_and_write<MAXC, METRIC>(g, t, sm, nc, alpha, lane);
+    if (kIncr && oldtrust != 0 &&
+        incremental_prune_and_write<(MAXC > 0 ? MAXC : 1)>(g, t, sm, incr, na, nc, alpha, lane,
+                                                           oldtrust)) {
+#ifdef JB_BUILD_CLOCKS
+      if (lane == 0) {
+        atomicAdd(&g_build_clk[4], 1ull);
+        atomicAdd(&g_build_clk[5], (unsigned long long)(clock64() - _c2));
+      }
+#endif
+    } else if (PASS == 1) {
+      if (lane == 0) deferred[atomicAdd(n_deferred, 1u)] = gi;
+    } else if (GRAM && nc <= kGramMax) {
+      gram_prune_and_write<METRIC>(g, t, sm, wbase + wbytes, nc, alpha, lane);
+    } else {
+      prune_and_write<MAXC, METRIC>(g, t, sm, nc, alpha, lane);
+    }
 #ifdef JB_BUILD_CLOCKS
     long long _c3 = clock64();
     if (lane == 0) {
@@ -940,6 +1176,7 @@ __global__ void __launch_bounds__(128) reverse_prune_kernel(GraphView g, const u
       atomicAdd(&g_build_clk[1], (unsigned long long)(_c2 - _c1));
       atomicAdd(&g_build_clk[2], (unsigned long long)(_c3 - _c2));
       atomicAdd(&g_build_clk[3], 1ull);
+      atomicAdd(&g_build_clk[6], (unsigned long long)nc);
     }
 #endif
   }
@@ -967,13 +1204,13 @@ struct Kernels {
     k<<<blocks, 128, smem, st>>>(g, off, bs, ws.vis_idx, ws.vis_dist, ws.vis_cnt, kBuildMaxResult,
                                  alpha);
   }
-  template <bool GRAM>
+  template <bool GRAM, int PASS>
   static void reverse_launch(const GraphView& g, size_t total, const BuildWorkspace& ws,
                              const uint64_t* sorted, float alpha, cudaStream_t st) {
-    const int warps = GRAM ? JB_GRAM_WARPS : 4;
-    const size_t smem = (prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) +
-                         (GRAM ? gram_warp_bytes(g.dpad) : 0)) * warps;
-    auto k = reverse_prune_kernel<MAXC, METRIC, GRAM>;
+    const int warps = PASS == 1 ? 4 : (GRAM ? JB_GRAM_WARPS : 4);
+    const size_t extra = PASS == 1 ? incr_scratch_bytes(g.dpad) : (GRAM ? gram_warp_bytes(g.dpad) : 0);
+    const size_t smem = (prune_warp_bytes(g.dpad, SelCache<MAXC, METRIC>::on) + extra) * warps;
+    auto k = reverse_prune_kernel<MAXC, METRIC, GRAM, PASS>;
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     int dev = 0, sms = 0, per_sm = 0;
     cudaGetDevice(&dev);
@@ -985,14 +1222,21 @@ struct Kernels {
     if (blocks > need) blocks = need;
     if (blocks == 0) blocks = 1;
     k<<<uint32_t(blocks), 32 * warps, smem, st>>>(g, sorted, total, ws.group_starts,
-                                                  ws.counters + 1, alpha);
+                                                  ws.counters + 1, alpha, ws.deferred,
+                                                  ws.counters + 2);
   }
   static void reverse(const GraphView& g, size_t total, const BuildWorkspace& ws,
                       const uint64_t* sorted, float alpha, cudaStream_t st) {
-    if (gram_prune_enabled() && g.dpad <= 128 && alpha > 0.f)
-      reverse_launch<true>(g, total, ws, sorted, alpha, st);
-    else
-      reverse_launch<false>(g, total, ws, sorted, alpha, st);
+    const bool gram = gram_prune_enabled() && g.dpad <= 128 && alpha > 0.f;
+    if (gram && g.eflag != nullptr && MAXC > 0 && METRIC == kL2) {
+      // incremental targets at high occupancy, then the rest with the Gram filter
+      reverse_launch<false, 1>(g, total, ws, sorted, alpha, st);
+      reverse_launch<true, 2>(g, total, ws, sorted, alpha, st);
+    } else if (gram) {
+      reverse_launch<true, 0>(g, total, ws, sorted, alpha, st);
+    } else {
+      reverse_launch<false, 0>(g, total, ws, sorted, alpha, st);
+    }
   }
 };
 
@@ -1018,7 +1262,7 @@ void dispatch_prune(const GraphView& g, uint32_t off, uint32_t bs, const BuildWo
 
 #ifdef JB_BUILD_CLOCKS
 extern "C" int jb_debug_build_clocks(unsigned long long* out) {
-  return cudaMemcpyFromSymbol(out, g_build_clk, sizeof(unsigned long long) * 4) == cudaSuccess ? 0 : 1;
+  return cudaMemcpyFromSymbol(out, g_build_clk, sizeof(unsigned long long) * 8) == cudaSuccess ? 0 : 1;
 }
 #endif
 
@@ -1046,6 +1290,7 @@ void workspace_allocate(BuildWorkspace& ws, uint32_t max_batch, uint32_t R) {
   check(cudaMalloc(&ws.rev_keys, pairs * 8), "alloc reverse pairs");
   check(cudaMalloc(&ws.rev_sorted, pairs * 8), "alloc sorted reverse pairs");
   check(cudaMalloc(&ws.group_starts, pairs * 4), "alloc group starts");
+  check(cudaMalloc(&ws.deferred, pairs * 4 + 4), "alloc deferred groups");
   check(cudaMalloc(&ws.counters, 256), "alloc counters");
   ws.sort_tmp_bytes = size_t(256) * ((pairs + kSortTile - 1) / kSortTile + 1) * 4;
   check(cudaMalloc(&ws.sort_tmp, ws.sort_tmp_bytes ? ws.sort_tmp_bytes : 16), "alloc sort counts");
@@ -1053,14 +1298,26 @@ void workspace_allocate(BuildWorkspace& ws, uint32_t max_batch, uint32_t R) {
 
 void workspace_free(BuildWorkspace& ws) {
   cudaFree(ws.vis_idx); cudaFree(ws.vis_dist); cudaFree(ws.vis_cnt);
-  cudaFree(ws.rev_keys); cudaFree(ws.rev_sorted); cudaFree(ws.group_starts);
+  cudaFree(ws.rev_keys); cudaFree(ws.rev_sorted); cudaFree(ws.group_starts); cudaFree(ws.deferred);
   cudaFree(ws.counters); cudaFree(ws.sort_tmp);
   ws = BuildWorkspace{};
 }
 
+// JB_INCR_PRUNE=0 in the environment turns the incremental reverse prune
+// (and the flags it keeps) off, for timing comparisons; the graphs are the
+// same either way.
+bool incr_prune_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("JB_INCR_PRUNE");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
 void process_batch(Graph& graph, BuildWorkspace& ws, uint32_t off, uint32_t bs, float alpha,
                    cudaStream_t st) {
-  const GraphView g = graph.view();
+  GraphView g = graph.view();
+  if (!incr_prune_enabled()) g.eflag = nullptr;
   check(cudaMemsetAsync(ws.counters, 0, 256, st), "clear counters");
   SearchArgs a{};
   a.g = g;
@@ -1087,6 +1344,15 @@ void process_batch(Graph& graph, BuildWorkspace& ws, uint32_t off, uint32_t bs, 
   if (g.metric == kIP) dispatch_prune<kIP>(g, off, bs, ws, alpha, st, true, total, sorted);
   else dispatch_prune<kL2>(g, off, bs, ws, alpha, st, true, total, sorted);
   check(cudaGetLastError(), "construct batch launch");
+}
+
+// The build's prune flags (GraphView::eflag), zero (nothing trusted) for
+// rows whose edges no prune of this process wrote.
+void ensure_prune_flags(Graph& g) {
+  if (g.eflag != nullptr || g.on_host) return;
+  const size_t rows = std::max<size_t>(g.capacity, 1);
+  check(cudaMalloc(&g.eflag, rows * 8), "alloc prune flags");
+  check(cudaMemset(g.eflag, 0, rows * 8), "clear prune flags");
 }
 
 // append_batch (include/jasper/index/construct.cuh:1169-1265): the new rows
@@ -1128,6 +1394,7 @@ std::vector<uint32_t> graph_append(Graph& graph, const uint16_t* rows, uint64_t 
   graph.n = uint32_t(new_n);
   graph.next_id += count;
   const uint32_t max_batch = uint32_t(std::min<uint64_t>(count, 100000));
+  ensure_prune_flags(graph);
   BuildWorkspace ws;
   workspace_allocate(ws, max_batch, graph.R);
   try {
@@ -1149,6 +1416,7 @@ std::vector<uint32_t> graph_append(Graph& graph, const uint16_t* rows, uint64_t 
 void construct_graph(Graph& graph, float alpha, uint32_t max_batch, cudaStream_t st) {
   if (max_batch == 0) max_batch = 1;
   if (graph.n == 0) return;
+  ensure_prune_flags(graph);
   BuildWorkspace ws;
   workspace_allocate(ws, max_batch, graph.R);
   try {

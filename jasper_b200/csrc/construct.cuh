@@ -20,7 +20,9 @@ struct BuildWorkspace {
   uint64_t* rev_keys = nullptr;    // [max_batch * R]
   uint64_t* rev_sorted = nullptr;  // [max_batch * R]
   uint32_t* group_starts = nullptr;
-  uint32_t* counters = nullptr;    // [0] search work counter, [1] reverse group count
+  uint32_t* deferred = nullptr;    // reverse groups left to the Gram pass
+  uint32_t* counters = nullptr;    // [0] search work counter, [1] reverse group count,
+                                   // [2] deferred group count
   void* sort_tmp = nullptr;        // semisort counts: [256][blocks of 4096 pairs], then 256 totals
   size_t sort_tmp_bytes = 0;
 };

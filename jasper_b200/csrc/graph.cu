@@ -118,6 +118,22 @@ void graph_reserve(Graph& g, uint32_t rows) {
       free_array(p, false);
     throw;
   }
+  if (g.eflag) {  // prune flags: the first n rows kept, the new ones zero
+    uint64_t* f = nullptr;
+    try {
+      f = alloc_array<uint64_t>(rows, false, "grow prune flags");
+      check(cudaMemcpy(f, g.eflag, n * 8, cudaMemcpyDeviceToDevice), "grow copy");
+      check(cudaMemset(f + n, 0, (rows - n) * 8), "grow memset");
+    } catch (...) {
+      free_array(f, false);
+      for (void* p : {static_cast<void*>(vec), static_cast<void*>(edges), static_cast<void*>(edist),
+                      static_cast<void*>(counts), static_cast<void*>(ids), static_cast<void*>(del)})
+        free_array(p, false);
+      throw;
+    }
+    cudaFree(g.eflag);
+    g.eflag = f;
+  }
   free_array(g.vec, false); free_array(g.edges, false); free_array(g.edist, false);
   free_array(g.counts, false); free_array(g.slot_to_id, false); free_array(g.deleted, false);
   g.vec = vec; g.edges = edges; g.edist = edist; g.counts = counts; g.slot_to_id = ids;
@@ -148,6 +164,8 @@ void graph_free(Graph& g) {
   free_array(g.counts, g.on_host);
   free_array(g.slot_to_id, g.on_host);
   free_array(g.deleted, g.on_host);
+  if (g.eflag) cudaFree(g.eflag);
+  g.eflag = nullptr;
   g.vec = nullptr; g.edges = nullptr; g.edist = nullptr; g.counts = nullptr;
   g.slot_to_id = nullptr; g.deleted = nullptr;
   g.n = 0;

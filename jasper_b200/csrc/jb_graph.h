@@ -38,6 +38,11 @@ struct GraphView {
   uint32_t global_offset;
   int metric;
   int ids_identity;
+  // Build only (null elsewhere): per row, bit e set when edge slot e was
+  // kept by a RobustPrune that tested it with exactly the distance stored
+  // for it (its bf16 value).  Lets a later re-prune of the row skip the
+  // pairs of two such edges (construct.cu, incremental prune).
+  uint64_t* eflag;
 };
 
 // Directional artifacts (reference: edge_lsh_list / edge_pq_list / lsh_globals
@@ -85,11 +90,12 @@ struct Graph {
   uint8_t* counts = nullptr;
   uint32_t* slot_to_id = nullptr;
   uint32_t* deleted = nullptr;
+  uint64_t* eflag = nullptr;   // build-time prune flags [capacity] (GraphView::eflag)
   DirArtifacts dir;
 
   GraphView view() const {
     return GraphView{vec, edges, edist, counts, slot_to_id, deleted, n, dim, dpad, R,
-                     medoid, global_offset, metric, ids_identity ? 1 : 0};
+                     medoid, global_offset, metric, ids_identity ? 1 : 0, eflag};
   }
 };
 
