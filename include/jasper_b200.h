@@ -107,9 +107,12 @@ int jb_graph_search_stats(int64_t handle, const uint16_t* queries, uint64_t n_qu
                           uint32_t beam_width, uint32_t limit, uint32_t* stats,
                           uint32_t* seen_scratch, void* stream);
 
-/* End-to-end search from host buffers: copies the queries in, searches and
- * copies the results back.  Synchronous (the reference's Search_ also
- * synchronises, beam_search.cuh:330). */
+/* End-to-end search from host buffers.  Page-locked (pinned) buffers are
+ * used in place: the search kernel reads each query row from host memory
+ * once and writes the results into host memory.  Pageable buffers, and
+ * query rows not at the padded stride (or not 16-byte aligned), go through
+ * device buffers with copies before and after the search.  Synchronous (the
+ * reference's Search_ also synchronises, beam_search.cuh:330). */
 int jb_graph_search_host(int64_t handle, const uint16_t* queries, uint64_t n_queries,
                          uint32_t row_stride, int32_t* out_idx, float* out_dist, uint32_t k,
                          uint32_t beam_width, uint32_t limit, void* stream);

@@ -143,10 +143,21 @@ void pool_alloc(void** p, size_t bytes, cudaStream_t st, const char* what) {
   cuda_check(cudaMallocFromPoolAsync(p, bytes, search_pool(), st), what);
 }
 
+// Device address of page-locked host memory mapped into the current
+// device's address space; null for pageable or device memory.
+void* mapped_host(const void* p) {
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
+}
+
 void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint32_t row_stride,
                  int32_t* out_idx, float* out_dist, uint32_t k, uint32_t bw, uint32_t limit,
                  uint32_t* stats, uint32_t* seen, cudaStream_t st, float rq_margin = -1.0f,
-                 bool rotate = false) {
+                 bool rotate = false, bool host_queries = false) {
   if (nq == 0) return;
   if (nq > 0x7FFFFFFFull) throw std::invalid_argument("too many queries");
   if (k == 0) throw std::invalid_argument("k must be > 0");
@@ -193,6 +204,9 @@ void search_impl(const jb::Graph& g, const uint16_t* queries, uint64_t nq, uint3
   a.stats = stats;
   a.seen_bits = seen;
   a.rot_pad = fused_rotation ? g.dir.rotation_pad : nullptr;
+  // queries still in page-locked host memory (not repacked): staged per row
+  a.stage_query = (host_queries && q == queries) ? 1 : 0;
+  if (a.stage_query && a.rot_pad != nullptr) throw std::logic_error("host queries on a prerotated graph");
   if (rq_margin >= 0.0f) {
     if (!g.dir.has_rabitq) throw std::runtime_error("graph has no RaBitQ codes built");
     if (!g.dir.rq_err)
@@ -331,33 +345,51 @@ int jb_graph_search_host(int64_t handle, const uint16_t* queries, uint64_t n_que
     auto g = lookup(handle);
     DeviceScope ds(g->device);
     if (n_queries == 0) return;
+    if (queries == nullptr || out_idx == nullptr || out_dist == nullptr)
+      throw std::invalid_argument("null pointer argument");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t qbytes = size_t(n_queries) * g->dpad * 2;
     const size_t obytes = size_t(n_queries) * k * 4;
+    // Page-locked buffers are used in place: the search kernel reads each
+    // query row over the host link once (16-byte loads staged in shared
+    // memory) and writes the results straight into host memory, so no copy
+    // sits before or after the search.  Pageable buffers (and query rows
+    // that are not at the padded stride, 16-byte aligned) go through device
+    // buffers and stream-ordered copies.
+    void* mq = mapped_host(queries);
+    void* mi = mapped_host(out_idx);
+    void* md = mapped_host(out_dist);
+    const bool q_direct = mq != nullptr && row_stride == g->dpad &&
+                          (reinterpret_cast<uintptr_t>(mq) % 16) == 0;
     void *dq = nullptr, *di = nullptr, *dd = nullptr;
     try {
-      pool_alloc(&dq, qbytes, st, "alloc queries");
-      pool_alloc(&di, obytes, st, "alloc out idx");
-      pool_alloc(&dd, obytes, st, "alloc out dist");
-      if (row_stride == g->dpad) {
-        cuda_check(cudaMemcpyAsync(dq, queries, qbytes, cudaMemcpyHostToDevice, st), "copy queries");
-      } else {
-        cuda_check(cudaMemsetAsync(dq, 0, qbytes, st), "clear queries");
-        cuda_check(cudaMemcpy2DAsync(dq, size_t(g->dpad) * 2, queries, size_t(row_stride) * 2,
-                                     size_t(g->dim) * 2, n_queries, cudaMemcpyHostToDevice, st),
-                   "copy queries");
+      if (!q_direct) {
+        pool_alloc(&dq, qbytes, st, "alloc queries");
+        if (row_stride == g->dpad) {
+          cuda_check(cudaMemcpyAsync(dq, queries, qbytes, cudaMemcpyHostToDevice, st), "copy queries");
+        } else {
+          cuda_check(cudaMemsetAsync(dq, 0, qbytes, st), "clear queries");
+          cuda_check(cudaMemcpy2DAsync(dq, size_t(g->dpad) * 2, queries, size_t(row_stride) * 2,
+                                       size_t(g->dim) * 2, n_queries, cudaMemcpyHostToDevice, st),
+                     "copy queries");
+        }
       }
-      search_impl(*g, static_cast<uint16_t*>(dq), n_queries, g->dpad, static_cast<int32_t*>(di),
-                  static_cast<float*>(dd), k, beam_width, limit, nullptr, nullptr, st);
-      cuda_check(cudaMemcpyAsync(out_idx, di, obytes, cudaMemcpyDeviceToHost, st), "copy idx");
-      cuda_check(cudaMemcpyAsync(out_dist, dd, obytes, cudaMemcpyDeviceToHost, st), "copy dist");
+      if (mi == nullptr) pool_alloc(&di, obytes, st, "alloc out idx");
+      if (md == nullptr) pool_alloc(&dd, obytes, st, "alloc out dist");
+      search_impl(*g, q_direct ? static_cast<const uint16_t*>(mq) : static_cast<uint16_t*>(dq),
+                  n_queries, g->dpad, static_cast<int32_t*>(mi ? mi : di),
+                  static_cast<float*>(md ? md : dd), k, beam_width, limit, nullptr, nullptr, st,
+                  -1.0f, false, q_direct);
+      if (di) cuda_check(cudaMemcpyAsync(out_idx, di, obytes, cudaMemcpyDeviceToHost, st), "copy idx");
+      if (dd) cuda_check(cudaMemcpyAsync(out_dist, dd, obytes, cudaMemcpyDeviceToHost, st), "copy dist");
     } catch (...) {
       for (void* p : {dq, di, dd})
         if (p) cudaFreeAsync(p, st);
       cudaStreamSynchronize(st);
       throw;
     }
-    cudaFreeAsync(dq, st); cudaFreeAsync(di, st); cudaFreeAsync(dd, st);
+    for (void* p : {dq, di, dd})
+      if (p) cudaFreeAsync(p, st);
     cuda_check(cudaStreamSynchronize(st), "search");
   });
 }

@@ -8,16 +8,16 @@
 // the summation order is the tensor core's, so outputs can differ from cuBLAS
 // in the last fp16 bit.
 //
-// One CTA of 128 threads per 128-row x BN-column output tile:
-//   thread 0     TMA producer: 64-wide K slices of X and M into a ring of
-//                SWIZZLE_128B stages (cp.async.bulk.tensor, no multicast);
-//   thread 32    MMA issuer: per slice four tcgen05.mma kind::f16 (K = 16
-//                each), fp32 accumulator in TMEM; tcgen05.commit frees the
-//                stage and finally signals the epilogue;
-//   all threads  epilogue: tcgen05.ld of the thread's accumulator row (TMEM
-//                lane = output row), round to fp16, store.
+// Persistent: one CTA per SM walks 128-row x BN-column output tiles (roles
+// at rotate_tc_kernel).  TMA brings 64-wide K slices of X and M into a ring
+// of SWIZZLE_128B stages (cp.async.bulk.tensor, no multicast); one thread
+// issues tcgen05.mma kind::f16 (K = 16 each) into one of two fp32 TMEM
+// accumulators; four epilogue warps drain the other accumulator with
+// tcgen05.ld (TMEM lane = output row), round to fp16 and store, so a tile's
+// epilogue overlaps the next tile's loads and MMAs.
 // Every mbarrier wait is bounded: on timeout the CTA records an error code,
-// waits (bounded) for its own bulk copies, frees its TMEM and returns.
+// waits (bounded) for its own bulk copies and MMAs, frees its TMEM and
+// returns.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -129,12 +129,26 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// bn: output columns per CTA (multiple of 16, <= 256); tmem_cols: power of
-// two >= bn; stages: ring depth.
-__global__ void __launch_bounds__(128, 1)
+// Persistent kernel: one CTA of 192 threads per SM walks the output tiles
+// t = blockIdx.x, blockIdx.x + gridDim.x, ... (tile t = row tile t / ncol,
+// column tile t % ncol, so consecutive tiles reuse the same rows from L2).
+//   warp 0, lane 0  TMA producer: the K slices of every tile, back to back,
+//                   into a ring of `stages` SWIZZLE_128B stages;
+//   warp 1, lane 0  MMA issuer: a tile's slices accumulate into one of two
+//                   TMEM accumulators (tiles alternate), tcgen05.commit frees
+//                   each stage and finally marks the accumulator full;
+//   warps 2..5      epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (its
+//                   rows of the tile), rounds to fp16, stores, and hands the
+//                   accumulator back; meanwhile the MMA fills the other one.
+// bn: output columns per tile (multiple of 16, <= 256); tmem_cols: power of
+// two >= bn (columns per accumulator; two are allocated).
+constexpr int kThreads = 192;
+
+__global__ void __launch_bounds__(kThreads, 1)
     rotate_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_m,
                      uint16_t* __restrict__ Y, uint32_t n, uint32_t dpad, uint32_t bn,
-                     uint32_t tmem_cols, uint32_t stages, uint32_t ksteps) {
+                     uint32_t tmem_cols, uint32_t stages, uint32_t ksteps, uint32_t ncol,
+                     uint32_t ntiles) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte aligned stage ring: A slices [stages][128 x 128 B], then B
   // slices [stages][bn x 128 B]; barriers and the TMEM address after them.
@@ -145,19 +159,23 @@ __global__ void __launch_bounds__(128, 1)
   unsigned char* b_ring = base + size_t(stages) * a_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(b_ring + size_t(stages) * b_bytes);
   uint64_t* empty = full + stages;
-  uint64_t* done = empty + stages;
+  uint64_t* acc_full = empty + stages;  // [2] MMA -> epilogue
+  uint64_t* acc_free = acc_full + 2;    // [2] epilogue -> MMA (4 warp arrivals)
+  uint64_t* done = acc_free + 2;        // every MMA of this CTA completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const uint32_t row0 = blockIdx.x * kBM, col0 = blockIdx.y * bn;
-
-  __shared__ uint32_t s_fail;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __shared__ volatile uint32_t s_fail;
   if (tid == 0) {
     // a CTA that starts after another one failed does nothing
     s_fail = *reinterpret_cast<volatile unsigned int*>(&g_tc_rotate_error) ? 1u : 0u;
     for (uint32_t s = 0; s < stages; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_free[b], 4);
     }
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -167,7 +185,7 @@ __global__ void __launch_bounds__(128, 1)
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(tmem_cols)
+                 "r"(2 * tmem_cols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -176,87 +194,117 @@ __global__ void __launch_bounds__(128, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  if (tid == 0) {
-    // producer
-    uint32_t issued = 0;
-    for (uint32_t k = 0; k < ksteps; k++) {
-      const uint32_t s = k % stages;
-      if (k >= stages && !mbar_wait(&empty[s], ((k / stages) - 1) & 1)) {
-        atomicExch(&g_tc_rotate_error, 1u);
-        s_fail = 1;
-        break;
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer
+      uint32_t issued = 0;
+      bool ok = true;
+      for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int row0 = int((t / ncol) * kBM), col0 = int((t % ncol) * bn);
+        for (uint32_t k = 0; k < ksteps; k++, issued++) {
+          const uint32_t s = issued % stages;
+          if (issued >= stages && !mbar_wait(&empty[s], ((issued / stages) - 1) & 1)) {
+            atomicExch(&g_tc_rotate_error, 1u);
+            s_fail = 1;
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], a_bytes + b_bytes);
+          tma_load_2d(a_ring + size_t(s) * a_bytes, &map_x, &full[s], int(k * kBK), row0);
+          tma_load_2d(b_ring + size_t(s) * b_bytes, &map_m, &full[s], int(k * kBK), col0);
+        }
       }
-      mbar_expect_tx(&full[s], a_bytes + b_bytes);
-      tma_load_2d(a_ring + size_t(s) * a_bytes, &map_x, &full[s], int(k * kBK), int(row0));
-      tma_load_2d(b_ring + size_t(s) * b_bytes, &map_m, &full[s], int(k * kBK), int(col0));
-      issued++;
+      // drain: every issued copy has landed before the CTA can leave
+      for (uint32_t k = (issued > stages ? issued - stages : 0); k < issued; k++)
+        if (!mbar_wait(&full[k % stages], (k / stages) & 1)) atomicExch(&g_tc_rotate_error, 2u);
     }
-    // drain: every issued copy has landed before the CTA can leave
-    for (uint32_t k = (issued > stages ? issued - stages : 0); k < issued; k++)
-      if (!mbar_wait(&full[k % stages], (k / stages) & 1)) atomicExch(&g_tc_rotate_error, 2u);
-  } else if (tid == 32) {
-    // MMA issuer
-    const uint32_t idesc = f16_idesc(bn);
-    bool ok = true;
-    for (uint32_t k = 0; k < ksteps; k++) {
-      const uint32_t s = k % stages;
-      if (!mbar_wait(&full[s], (k / stages) & 1)) {
-        atomicExch(&g_tc_rotate_error, 3u);
-        ok = false;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer
+      const uint32_t idesc = f16_idesc(bn);
+      uint32_t consumed = 0, it = 0;
+      bool ok = true;
+      for (uint32_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, it++) {
+        const uint32_t b = it & 1;
+        // the epilogue has read this accumulator's previous tile
+        if (it >= 2 && (s_fail || !mbar_wait(&acc_free[b], ((it >> 1) - 1) & 1))) {
+          atomicExch(&g_tc_rotate_error, 5u);
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t acc = tmem + b * tmem_cols;
+        for (uint32_t k = 0; k < ksteps; k++, consumed++) {
+          const uint32_t s = consumed % stages;
+          if (!mbar_wait(&full[s], (consumed / stages) & 1)) {
+            atomicExch(&g_tc_rotate_error, 3u);
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint64_t ad = sw128_desc(a_ring + size_t(s) * a_bytes);
+          const uint64_t bd = sw128_desc(b_ring + size_t(s) * b_bytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; kk++)  // 32 bytes of K per MMA: +2 in the address field
+            mma_f16(acc, ad + 2ull * kk, bd + 2ull * kk, idesc, (k | kk) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(&acc_full[b]);
+      }
+      if (!ok) s_fail = 1;
+      mma_commit(done);  // arrives once every MMA issued above has completed
+      if (!mbar_wait(done, 0)) atomicExch(&g_tc_rotate_error, 6u);
+    }
+  } else {
+    // epilogue: TMEM lane quadrant of this warp = its rows within the tile
+    const uint32_t quad = uint32_t(warp & 3);
+    const uint32_t lane_base = (quad * 32) << 16;
+    uint32_t it = 0;
+    for (uint32_t t = blockIdx.x; t < ntiles; t += gridDim.x, it++) {
+      const uint32_t b = it & 1;
+      // warp-uniform wait (tcgen05.ld below is warp-collective)
+      int ok = 1;
+      if (lane == 0) ok = !s_fail && mbar_wait(&acc_full[b], (it >> 1) & 1);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        if (lane == 0) atomicExch(&g_tc_rotate_error, 4u);
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint64_t ad = sw128_desc(a_ring + size_t(s) * a_bytes);
-      const uint64_t bd = sw128_desc(b_ring + size_t(s) * b_bytes);
+      const uint32_t r = (t / ncol) * kBM + quad * 32 + uint32_t(lane);
+      const uint32_t col0 = (t % ncol) * bn;
+      for (uint32_t c = 0; c < bn; c += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + lane_base + b * tmem_cols + c, v);
+        if (r < n && col0 + c < dpad) {
+          uint32_t w[8];
 #pragma unroll
-      for (int kk = 0; kk < kBK / 16; kk++)  // 32 bytes of K per MMA: +2 in the address field
-        mma_f16(tmem, ad + 2ull * kk, bd + 2ull * kk, idesc, (k | kk) ? 1u : 0u);
-      mma_commit(&empty[s]);
-    }
-    if (!ok) s_fail = 1;
-    mma_commit(done);  // arrives once every MMA issued above has completed
-  }
-  __syncwarp();
-  // epilogue (all 128 threads): thread t owns TMEM lane t = output row row0 + t
-  int failed = (tid == 0 || tid == 32) ? int(s_fail) : 0;
-  if (!mbar_wait(done, 0)) {
-    atomicExch(&g_tc_rotate_error, 4u);
-    failed = 1;
-  }
-  // CTA-uniform decision: tcgen05.ld below is warp-collective
-  failed = __syncthreads_or(failed);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (!failed) {
-    const uint32_t r = row0 + uint32_t(tid);
-    const uint32_t lane_base = uint32_t(warp * 32) << 16;
-    for (uint32_t c = 0; c < bn; c += 16) {
-      uint32_t v[16];
-      tmem_ld16(tmem + lane_base + c, v);
-      if (r < n && col0 + c < dpad) {
-        uint32_t w[8];
+          for (int j = 0; j < 8; j++) {
+            const __half2 h2 = __floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+            w[j] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          uint16_t* dst = Y + size_t(r) * dpad + col0 + c;
+          if (col0 + c + 16 <= dpad) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst);
+            d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          } else {
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          const __half2 h2 = __floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-          w[j] = *reinterpret_cast<const uint32_t*>(&h2);
-        }
-        uint16_t* dst = Y + size_t(r) * dpad + col0 + c;
-        if (col0 + c + 16 <= dpad) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst);
-          d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-          d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        } else {
-#pragma unroll
-          for (uint32_t j = 0; j < 16; j++)
-            if (col0 + c + j < dpad) dst[j] = uint16_t(w[j >> 1] >> (16 * (j & 1)));
+            for (uint32_t j = 0; j < 16; j++)
+              if (col0 + c + j < dpad) dst[j] = uint16_t(w[j >> 1] >> (16 * (j & 1)));
+          }
         }
       }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_free[b])) : "memory");
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(tmem_cols)
+                 "r"(2 * tmem_cols)
                  : "memory");
 }
 
@@ -303,22 +351,30 @@ void rotate_rows_tc(const uint16_t* Mp, uint32_t dpad, const uint16_t* X, uint16
        reinterpret_cast<uintptr_t>(Mp)) % 16)
     throw std::invalid_argument("rotate: buffers must be 16-byte aligned");
   // N tiles of at most 256 columns (multiple of 16)
-  const uint32_t ntiles = (dpad + 255) / 256;
-  uint32_t bn = (dpad + ntiles - 1) / ntiles;
+  const uint32_t nsplit = (dpad + 255) / 256;
+  uint32_t bn = (dpad + nsplit - 1) / nsplit;
   bn = (bn + 15) / 16 * 16;
   uint32_t tmem_cols = 32;
   while (tmem_cols < bn) tmem_cols <<= 1;
   const uint32_t ksteps = (dpad + kBK - 1) / kBK;
   const size_t stage_bytes = size_t(kBM) * 128 + size_t(bn) * 128;
-  uint32_t stages = ksteps < 4 ? ksteps : 4;
-  while (stages > 1 && stages * stage_bytes + 2048 > 200 * 1024) stages--;
-  const size_t smem = stages * stage_bytes + 1024 /* alignment */ + 8 * (2 * stages + 1) + 16;
+  // ring depth: up to 6 stages in one CTA's shared memory (one CTA per SM)
+  uint32_t stages = 6;
+  while (stages > 2 && stages * stage_bytes + 2048 > 220 * 1024) stages--;
+  const size_t smem = stages * stage_bytes + 1024 /* alignment */ + 8 * (2 * stages + 5) + 16;
   const CUtensorMap mx = make_map(X, n, dpad, dpad, kBM);
   const CUtensorMap mm = make_map(Mp, dpad, dpad, dpad, bn);
   cudaFuncSetAttribute(rotate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-  const dim3 grid(uint32_t((n + kBM - 1) / kBM), (dpad + bn - 1) / bn);
-  rotate_tc_kernel<<<grid, 128, smem, st>>>(mx, mm, Y, uint32_t(n), dpad, bn, tmem_cols, stages,
-                                            ksteps);
+  const uint32_t ncol = (dpad + bn - 1) / bn;
+  const uint64_t ntiles64 = ((n + kBM - 1) / kBM) * uint64_t(ncol);
+  if (ntiles64 >= (uint64_t(1) << 31)) throw std::invalid_argument("rotate: too many tiles");
+  const uint32_t ntiles = uint32_t(ntiles64);
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint32_t grid = ntiles < uint32_t(sms > 0 ? sms : 1) ? ntiles : uint32_t(sms);
+  rotate_tc_kernel<<<grid, kThreads, smem, st>>>(mx, mm, Y, uint32_t(n), dpad, bn, tmem_cols,
+                                                 stages, ksteps, ncol, ntiles);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("rotate launch: ") + cudaGetErrorString(e));
 }

@@ -479,6 +479,17 @@ __device__ __forceinline__ void prefetch_edges(const GraphView& g, uint32_t id) 
   prefetch_l2(g.counts + l);
 }
 
+// Stages one query row from page-locked host memory into shared memory:
+// 16-byte loads, lanes on consecutive chunks (each row crosses the host link
+// once, in a few wide requests).  Plain loads: the non-coherent path is kept
+// for device memory.
+__device__ __forceinline__ void stage_query_row(uint16_t* dst, const uint16_t* src, int nchunks,
+                                                int lane, int nthreads) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+  for (int c = lane; c < nchunks; c += nthreads) d4[c] = s4[c];
+}
+
 #ifndef JB_SEARCH_MIN_BLOCKS
 #define JB_SEARCH_MIN_BLOCKS 4
 #endif
@@ -552,6 +563,15 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC, BWCAP>())
       rotate_query_warp(raw, rot, a.rot_pad, g.dim, dpad, lane);
       __syncwarp();
       qrow = rot;
+      q_in_smem = true;
+    } else if (a.stage_query) {
+      // Host-resident query: the register layouts build from a copy in the
+      // visited table's slots (cleared below); the shared-memory layout
+      // keeps it in sm.query.
+      uint16_t* dst = kRegQ ? reinterpret_cast<uint16_t*>(sm.hash) : sm.query;
+      stage_query_row(dst, qrow, nchunks, lane, 32);
+      __syncwarp();
+      qrow = dst;
       q_in_smem = true;
     }
     if constexpr (kTile) {
@@ -1067,6 +1087,12 @@ __global__ void __launch_bounds__(32 * W, 16 / W) beam_search_cta_kernel(SearchA
         rotate_query_warp(raw, rot, a.rot_pad, g.dim, dpad, lane);
         __syncwarp();
         qrow = rot;
+      } else if (a.stage_query) {
+        // Host-resident query (see the warp kernel)
+        uint16_t* dst = kTile ? reinterpret_cast<uint16_t*>(sm.hash) : sm.query;
+        stage_query_row(dst, qrow, nchunks, lane, 32);
+        __syncwarp();
+        qrow = dst;
       } else if constexpr (!kTile) {
         const uint4* src = reinterpret_cast<const uint4*>(qrow);
         for (int c = lane; c < nchunks; c += 32) reinterpret_cast<uint4*>(sm.query)[c] = ldg16(src + c);

@@ -40,6 +40,10 @@ struct SearchArgs {
   // dpad fp16, row i = column i of P; the kernel rotates each query in its
   // prologue.  Needs dpad <= kFusedRotationMaxDpad.
   const uint16_t* rot_pad;
+  // Queries in page-locked host memory (read over the host link): each row
+  // is read once, with 16-byte loads, into shared memory before any use.
+  // Not combined with rot_pad.
+  int stage_query;
 };
 
 // Largest padded dimension whose query rotation fits the prologue's scratch.

@@ -48,7 +48,8 @@ def test_r_diagonal_sign_convention():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("dim,n", [(128, 20000), (96, 3000), (200, 5000), (960, 2000), (40, 700)])
+@pytest.mark.parametrize("dim,n", [(128, 20000), (96, 3000), (200, 5000), (960, 2000), (40, 700),
+                                   (256, 40000), (960, 12000), (128, 300000)])
 def test_tensor_core_rotation_matches_reference_gemm(cuda, dim, n):
     """tcgen05 rotation GEMM vs the SIMT fp32-accumulate GEMM and a float64
     product of the same fp16 operands.  Tolerance per output: 1 fp16 ulp of
