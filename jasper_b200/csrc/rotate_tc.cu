@@ -10,7 +10,7 @@
 //
 // Persistent: one CTA per SM walks 128-row x BN-column output tiles (roles
 // at rotate_tc_kernel).  TMA brings 64-wide K slices of X and M into a ring
-// of SWIZZLE_128B stages (cp.async.bulk.tensor, no multicast); one thread
+// of SWIZZLE_128B stages (cp.async.bulk.tensor, each CTA its own tiles); one thread
 // issues tcgen05.mma kind::f16 (K = 16 each) into one of two fp32 TMEM
 // accumulators; four epilogue warps drain the other accumulator with
 // tcgen05.ld (TMEM lane = output row), round to fp16 and store, so a tile's
