@@ -880,7 +880,23 @@ __global__ void __launch_bounds__(128, search_min_blocks<MAXC, METRIC, BWCAP>())
       // Merge beam (cnt) and kept candidates by rank; keep the first bw.
       // A few kept candidates stay unsorted: each position is counted
       // directly (keys are distinct, so every rank is exact).
-      if (kept <= kCountMerge) {
+      if (BWCAP <= 32 && kept <= kCountMerge) {
+        // beam of at most 32: one pass over the kept keys counts both the
+        // beam entry's rank among them and the lane's own candidate's
+        const uint64_t b = lane < int(cnt) ? cur[lane] : kKeyMax;
+        const uint64_t c = lane < kept ? sm.cand_keys[lane] : kKeyMax;
+        uint32_t rb = 0, rc = 0;
+        for (int j = 0; j < kept; j++) {
+          const uint64_t t = sm.cand_keys[j];
+          rb += t < b;
+          rc += t < c;
+        }
+        if (lane < int(cnt) && lane + rb < bw) nxt[lane + rb] = b;
+        if (lane < kept) {
+          const uint32_t p = rc + lower_rank(cur, int(cnt), c);
+          if (p < bw) nxt[p] = c;
+        }
+      } else if (kept <= kCountMerge) {
         for (uint32_t i = lane; i < cnt; i += 32) {
           const uint64_t b = cur[i];
           uint32_t r = 0;
