@@ -13,8 +13,9 @@
 // of SWIZZLE_128B stages (cp.async.bulk.tensor, each CTA its own tiles); one thread
 // issues tcgen05.mma kind::f16 (K = 16 each) into one of two fp32 TMEM
 // accumulators; four epilogue warps drain the other accumulator with
-// tcgen05.ld (TMEM lane = output row), round to fp16 and store, so a tile's
-// epilogue overlaps the next tile's loads and MMAs.
+// tcgen05.ld (TMEM lane = output row), round to fp16, stage 32-row x
+// 16-column boxes in shared memory and store them with TMA bulk tensor
+// stores, so a tile's epilogue overlaps the next tile's loads and MMAs.
 // Every mbarrier wait is bounded: on timeout the CTA records an error code,
 // waits (bounded) for its own bulk copies and MMAs, frees its TMEM and
 // returns.
@@ -138,15 +139,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 //                   TMEM accumulators (tiles alternate), tcgen05.commit frees
 //                   each stage and finally marks the accumulator full;
 //   warps 2..5      epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 (its
-//                   rows of the tile), rounds to fp16, stores, and hands the
-//                   accumulator back; meanwhile the MMA fills the other one.
+//                   rows of the tile), rounds to fp16 into its staging boxes,
+//                   hands the accumulator back and issues the boxes' TMA
+//                   stores; meanwhile the MMA fills the other accumulator.
 // bn: output columns per tile (multiple of 16, <= 256); tmem_cols: power of
 // two >= bn (columns per accumulator; two are allocated).
 constexpr int kThreads = 192;
 
 __global__ void __launch_bounds__(kThreads, 1)
     rotate_tc_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_m,
-                     uint16_t* __restrict__ Y, uint32_t n, uint32_t dpad, uint32_t bn,
+                     const __grid_constant__ CUtensorMap map_y, uint32_t n, uint32_t dpad, uint32_t bn,
                      uint32_t tmem_cols, uint32_t stages, uint32_t ksteps, uint32_t ncol,
                      uint32_t ntiles) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -157,7 +159,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t a_bytes = kBM * 128, b_bytes = bn * 128;
   unsigned char* a_ring = base;
   unsigned char* b_ring = base + size_t(stages) * a_bytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(b_ring + size_t(stages) * b_bytes);
+  // epilogue staging: per epilogue warp, bn / 16 boxes of 32 rows x 16 columns
+  unsigned char* y_stage = b_ring + size_t(stages) * b_bytes;
+  const uint32_t y_warp_bytes = bn * 64;
+  uint64_t* full = reinterpret_cast<uint64_t*>(y_stage + size_t(4) * y_warp_bytes);
   uint64_t* empty = full + stages;
   uint64_t* acc_full = empty + stages;  // [2] MMA -> epilogue
   uint64_t* acc_free = acc_full + 2;    // [2] epilogue -> MMA (4 warp arrivals)
@@ -271,34 +276,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t r = (t / ncol) * kBM + quad * 32 + uint32_t(lane);
-      const uint32_t col0 = (t % ncol) * bn;
+      const int y0 = int((t / ncol) * kBM + quad * 32);
+      const int x0 = int((t % ncol) * bn);
+      unsigned char* stage_w = y_stage + size_t(warp - 2) * y_warp_bytes;
+      // the previous tile's stores have finished reading this warp's staging
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      __syncwarp();
       for (uint32_t c = 0; c < bn; c += 16) {
         uint32_t v[16];
         tmem_ld16(tmem + lane_base + b * tmem_cols + c, v);
-        if (r < n && col0 + c < dpad) {
-          uint32_t w[8];
+        uint32_t w[8];
 #pragma unroll
-          for (int j = 0; j < 8; j++) {
-            const __half2 h2 = __floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-            w[j] = *reinterpret_cast<const uint32_t*>(&h2);
-          }
-          uint16_t* dst = Y + size_t(r) * dpad + col0 + c;
-          if (col0 + c + 16 <= dpad) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst);
-            d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
-          } else {
-#pragma unroll
-            for (uint32_t j = 0; j < 16; j++)
-              if (col0 + c + j < dpad) dst[j] = uint16_t(w[j >> 1] >> (16 * (j & 1)));
-          }
+        for (int j = 0; j < 8; j++) {
+          const __half2 h2 = __floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+          w[j] = *reinterpret_cast<const uint32_t*>(&h2);
         }
+        // box c / 16: 32 rows x 16 columns, row `lane` at byte 32 * lane
+        uint4* d4 = reinterpret_cast<uint4*>(stage_w + (c / 16) * 1024 + lane * 32);
+        d4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        d4[1] = make_uint4(w[4], w[5], w[6], w[7]);
       }
+      // TMEM reads done: hand the accumulator back before the stores
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       __syncwarp();
-      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_free[b])) : "memory");
+      if (lane == 0) {
+        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_free[b])) : "memory");
+        // rows past n and columns past dpad are clipped by the tensor map;
+        // x is a multiple of 16 elements (32 bytes), never negative
+        for (uint32_t c = 0; c < bn && x0 + int(c) < int(dpad) && y0 < int(n); c += 16)
+          asm volatile(
+              "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                  reinterpret_cast<uint64_t>(&map_y)),
+              "r"(x0 + int(c)), "r"(y0), "r"(smem_u32(stage_w + (c / 16) * 1024))
+              : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
     }
+    // every store of this warp has completed before the CTA leaves
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
@@ -324,16 +341,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D fp16 map over rows x cols (row stride `stride` elements), box of
 // box_rows x 64 with 128-byte swizzle; out-of-range elements read as zero.
+// box_cols = 64 with the 128-byte swizzle for the operand loads; the output
+// map uses unswizzled 16-column boxes.
 CUtensorMap make_map(const void* ptr, uint64_t rows, uint64_t cols, uint64_t stride,
-                     uint32_t box_rows) {
+                     uint32_t box_rows, uint32_t box_cols = kBK,
+                     CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   CUtensorMap m;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {stride * 2};
-  const cuuint32_t box[2] = {uint32_t(kBK), box_rows};
+  const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr),
                                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                 swz, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     throw std::runtime_error("cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
@@ -359,11 +379,14 @@ void rotate_rows_tc(const uint16_t* Mp, uint32_t dpad, const uint16_t* X, uint16
   const uint32_t ksteps = (dpad + kBK - 1) / kBK;
   const size_t stage_bytes = size_t(kBM) * 128 + size_t(bn) * 128;
   // ring depth: up to 6 stages in one CTA's shared memory (one CTA per SM)
+  const size_t ystage_bytes = size_t(4) * bn * 64;  // epilogue staging, 4 warps
   uint32_t stages = 6;
-  while (stages > 2 && stages * stage_bytes + 2048 > 220 * 1024) stages--;
-  const size_t smem = stages * stage_bytes + 1024 /* alignment */ + 8 * (2 * stages + 5) + 16;
+  while (stages > 2 && stages * stage_bytes + ystage_bytes + 2048 > 220 * 1024) stages--;
+  const size_t smem =
+      stages * stage_bytes + ystage_bytes + 1024 /* alignment */ + 8 * (2 * stages + 5) + 16;
   const CUtensorMap mx = make_map(X, n, dpad, dpad, kBM);
   const CUtensorMap mm = make_map(Mp, dpad, dpad, dpad, bn);
+  const CUtensorMap my = make_map(Y, n, dpad, dpad, 32, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
   cudaFuncSetAttribute(rotate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   const uint32_t ncol = (dpad + bn - 1) / bn;
   const uint64_t ntiles64 = ((n + kBM - 1) / kBM) * uint64_t(ncol);
@@ -373,7 +396,7 @@ void rotate_rows_tc(const uint16_t* Mp, uint32_t dpad, const uint16_t* X, uint16
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const uint32_t grid = ntiles < uint32_t(sms > 0 ? sms : 1) ? ntiles : uint32_t(sms);
-  rotate_tc_kernel<<<grid, kThreads, smem, st>>>(mx, mm, Y, uint32_t(n), dpad, bn, tmem_cols,
+  rotate_tc_kernel<<<grid, kThreads, smem, st>>>(mx, mm, my, uint32_t(n), dpad, bn, tmem_cols,
                                                  stages, ksteps, ncol, ntiles);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("rotate launch: ") + cudaGetErrorString(e));
