@@ -23,7 +23,10 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <map>
+#include <mutex>
 #include <stdexcept>
+#include <utility>
 #include <string>
 #include "rotate.cuh"
 
@@ -387,14 +390,26 @@ void rotate_rows_tc(const uint16_t* Mp, uint32_t dpad, const uint16_t* X, uint16
   const CUtensorMap mx = make_map(X, n, dpad, dpad, kBM);
   const CUtensorMap mm = make_map(Mp, dpad, dpad, dpad, bn);
   const CUtensorMap my = make_map(Y, n, dpad, dpad, 32, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
-  cudaFuncSetAttribute(rotate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  int dev = 0;
+  cudaGetDevice(&dev);
+  // per device: the SM count, and the largest shared-memory opt-in made so far
+  static std::mutex mu;
+  static std::map<int, std::pair<int, size_t>> dev_state;
+  int sms = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto& st_dev = dev_state[dev];
+    if (st_dev.first == 0) cudaDeviceGetAttribute(&st_dev.first, cudaDevAttrMultiProcessorCount, dev);
+    if (smem > st_dev.second) {
+      cudaFuncSetAttribute(rotate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+      st_dev.second = smem;
+    }
+    sms = st_dev.first;
+  }
   const uint32_t ncol = (dpad + bn - 1) / bn;
   const uint64_t ntiles64 = ((n + kBM - 1) / kBM) * uint64_t(ncol);
   if (ntiles64 >= (uint64_t(1) << 31)) throw std::invalid_argument("rotate: too many tiles");
   const uint32_t ntiles = uint32_t(ntiles64);
-  int dev = 0, sms = 0;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const uint32_t grid = ntiles < uint32_t(sms > 0 ? sms : 1) ? ntiles : uint32_t(sms);
   rotate_tc_kernel<<<grid, kThreads, smem, st>>>(mx, mm, my, uint32_t(n), dpad, bn, tmem_cols,
                                                  stages, ksteps, ncol, ntiles);
