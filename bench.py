@@ -52,7 +52,7 @@ sys.path.insert(0, str(ROOT))
 BWS = (16, 32, 64, 128, 256)
 # DRAM bytes (read + write) of one search launch, from an ncu capture of this
 # bench's own launch: (rows, queries, beam width) -> bytes.
-SEARCH_TRAFFIC = {(1_000_000, 10_000, 32): 1_715_190_608}
+SEARCH_TRAFFIC = {(1_000_000, 10_000, 32): 1_719_287_344}
 TARGET = 0.95
 K = 10
 METRIC = "QPS at recall@10=0.95 and build Mvec/s, 1M×128 fp16, at 1/2/4/8 B200"
