@@ -144,5 +144,35 @@ class ShardedGraph:
             phases.append(ev)
         return out
 
+    def search_host(self, queries: torch.Tensor, out_idx: torch.Tensor, out_dist: torch.Tensor,
+                    k: int = 10, beam_width: int = 64, root: int = 0) -> bool:
+        """search() from host buffers: ``queries`` [nq, dim] fp16 and, on
+        ``root``, ``out_idx`` / ``out_dist`` [nq, k] on the host (page-locked
+        for speed).  With one shard the C ABI's host-buffer search runs (the
+        kernel reads page-locked queries and writes the results in place);
+        with several, the queries are uploaded asynchronously, searched,
+        exchanged and merged, and the merged top-k is copied into the output
+        buffers.  Synchronous; returns True on ``root``."""
+        import torch.distributed as dist
+        world = dist.get_world_size(self.group) if dist.is_initialized() else 1
+        if queries.is_cuda or out_idx.is_cuda or out_dist.is_cuda:
+            raise ValueError("search_host takes host tensors")
+        q = queries.contiguous()
+        if world == 1:
+            if not (out_idx.is_contiguous() and out_dist.is_contiguous()):
+                raise ValueError("output buffers must be contiguous")
+            limit = beam_width * 2
+            _lib.call("jb_graph_search_host", self.graph._handle, q.data_ptr(), q.shape[0],
+                      q.shape[1], out_idx.data_ptr(), out_dist.data_ptr(), k, beam_width, limit,
+                      torch.cuda.current_stream().cuda_stream)
+            return True
+        dev = torch.device("cuda", torch.cuda.current_device())
+        res = self.search(q.to(dev, non_blocking=True), k=k, beam_width=beam_width, root=root)
+        if res is not None:
+            out_idx.copy_(res[0], non_blocking=True)
+            out_dist.copy_(res[1], non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return res is not None
+
     def free(self):
         self.graph.free()

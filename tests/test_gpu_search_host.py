@@ -78,3 +78,28 @@ def test_search_host_large_batch(cuda):
                 T.assert_same_results(gi, gd, ri, rd, msg=f"pinned={pinned}")
     finally:
         T.free(h)
+
+
+@pytest.mark.parametrize("dim", [200, 960])
+@pytest.mark.parametrize("metric", [0, 1])
+def test_search_host_pinned_wide_rows(cuda, dim, metric):
+    """Page-locked buffers are read and written in place by the search
+    kernel, which stages each query row in shared memory before building its
+    query layout: the lane-per-row layout (dim 200) and the shared-memory
+    query (dim 960), for both the warp-per-query kernel (2500 queries) and
+    the CTA-per-query kernel (300 queries)."""
+    n, k, bw = 3000, 10, 32
+    X = synthetic.gaussian(n, dim, 81 + dim)
+    h = T.construct(X, 16, metric, 1.2 if metric == 0 else 1.0)
+    try:
+        for nq in (2500, 300):
+            Q = synthetic.gaussian(nq, dim, 82 + dim)
+            ri, rd = T.search(h, Q, k, bw)
+            q = torch.from_numpy(O.pad_rows(Q)).pin_memory()
+            oi = torch.full((nq, k), 7, dtype=torch.int32).pin_memory()
+            od = torch.full((nq, k), 7.0, dtype=torch.float32).pin_memory()
+            for _ in range(2):
+                gi, gd = _host_search(h, q, k, bw, oi, od)
+                T.assert_same_results(gi, gd, ri, rd, msg=f"dim={dim} nq={nq}")
+    finally:
+        T.free(h)
